@@ -1,0 +1,381 @@
+#!/usr/bin/env python
+"""Benchmark of the sparse-attention hot path: graph build + gather attention
+forward (the reference's "fwd+graph" metric) on one of the BASELINE
+workloads, default the headline GQA config c2 (B=4, N=8192, 32 q / 8 kv
+heads, d=128, K=128, bf16).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2]
+    python bench.py --impl reference ...     # CPU reference arm (oracle port)
+
+One step = SparseAttention's graph build (hash, buckets, candidate scan +
+top-k, merge) and gather attention over q/k/v already resident in HBM.
+Under torchrun each rank runs its own full batch of the workload (weak
+scaling: the path has no cross-rank exchange for this sharding); the step
+time is the maximum over ranks. L2 is flushed (a 256 MB write) between timed
+steps; every step is timed with CUDA events on the launching stream.
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import datetime
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "sparse-attn fwd+graph tokens/s/GPU at N=8192,K=128; % HBM roofline"
+PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_HBM_GBS = 6650.0
+TRAFFIC_FILE = os.path.join(ROOT, "profiles", "traffic.json")
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c5"])
+    ap.add_argument("--impl", default="ssa", choices=["ssa", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--baseline-slices", type=int, default=2,
+                    help="(batch, kv-group) slices in the CPU baseline sample")
+    return ap.parse_args(argv)
+
+
+def hbm_peak():
+    try:
+        with open(PEAKS_FILE) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="ssa_clocks_", suffix=".csv")
+            os.close(fd)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        rows = []
+        with open(self.path) as f:
+            for r in csv.reader(f):
+                if len(r) >= 9:
+                    rows.append([x.strip() for x in r])
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def dist_info():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle port on a bounded sample of the same workload
+# ---------------------------------------------------------------------------
+def cpu_sample(w, m, q, k, v, slices: int):
+    """Runs the oracle's build_graph + attention forward on `slices`
+    (batch, kv-group) slices; returns (seconds, description, threads)."""
+    from oracle import oracle as O
+    rep = w.H // w.n_kv
+    lsh = m.lsh_builder
+    rp = lsh.rand_proj.detach().cpu().float().numpy()
+    glob_idx = list(w.glob) if w.glob else None
+    work = []
+    for s in range(slices):
+        b, g = divmod(s, w.n_kv)
+        b = b % w.B
+        work.append((q[b:b + 1, g * rep:(g + 1) * rep].float().contiguous().cpu().numpy(),
+                     k[b:b + 1, g:g + 1].float().contiguous().cpu().numpy(),
+                     v[b:b + 1, g:g + 1].float().contiguous().cpu().numpy()))
+    t0 = time.perf_counter()
+    for qs, ks, vs in work:
+        nb, va = O.build_graph(qs, ks, rp, n_kv=1, K=w.K, w=w.window, G=w.G, glob_idx=glob_idx,
+                               R=w.R, maxP=w.max_p, T=w.T, causal=w.causal, is_cross=w.cross)
+        O.attn_fwd(qs, ks, vs, nb, va, scale=w.d ** -0.5, lowp=w.dtype == "bf16", fp32_w=False)
+    dt = time.perf_counter() - t0
+    desc = (f"{slices} of {w.B * w.n_kv} (batch, kv-group) slices ({rep} q heads x {w.N} queries "
+            f"each) of {w.name}; full-job time extrapolated linearly in slices")
+    return dt, desc, O.num_threads()
+
+
+def cpu_baseline_value(w, dt, slices):
+    full = dt * (w.B * w.n_kv) / slices
+    return w.B * w.N / full, full
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    from ssa_b200 import ops
+    from ssa_b200.workloads import WORKLOADS, make_module, make_x, project
+
+    world, rank, local = dist_info()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    w = WORKLOADS[args.workload]
+    m = make_module(w, dev)
+    x, kv = make_x(w, dev, seed=1 + rank)
+    q, k, v = project(m, x, kv)
+    del x, kv
+    causal = w.causal and not w.cross
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        nb, valid = m._graph(q, k, w.M, causal, w.cross)
+        e_mid = torch.cuda.Event(enable_timing=True)
+        e_mid.record(stream)
+        out, _ = ops.attn_fwd(q, k, v, nb, valid, m.scale, False, want_lse=False)
+        return out, e_mid
+
+    with torch.no_grad():
+        for _ in range(max(args.warmup, 0)):
+            flush.zero_()
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        clocks = ClockSampler(local)
+        clocks.start()
+        torch.cuda.synchronize()
+        evs = []
+        for _ in range(args.steps):
+            flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e2 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            out, e1 = step()
+            e2.record(stream)
+            evs.append((e0, e1, e2))
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        clk = clocks.stop()
+    tot = [a.elapsed_time(c) for a, b, c in evs]
+    graph = [a.elapsed_time(b) for a, b, c in evs]
+    attn = [b.elapsed_time(c) for a, b, c in evs]
+    ms = statistics.mean(tot)
+    ms_graph, ms_attn = statistics.mean(graph), statistics.mean(attn)
+    if world > 1:
+        t = torch.tensor([ms, ms_graph, ms_attn], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ms_graph, ms_attn = [float(x) for x in t.tolist()]
+
+    tokens = w.B * w.N
+    value = world * tokens / (ms / 1e3)
+    peak, peak_src = hbm_peak()
+    alg_bytes = w.bytes_per_token() * tokens
+    attn_gbs = alg_bytes / (ms_attn / 1e3) / 1e9
+    step_gbs = alg_bytes / (ms / 1e3) / 1e9
+    traffic = None
+    try:
+        with open(TRAFFIC_FILE) as f:
+            traffic = json.load(f).get(w.name, {}).get("k_attn_fwd")
+    except Exception:
+        pass
+
+    # End to end through the public API with host buffers: pinned q/k/v in,
+    # attention output back to pinned host memory, copies inside the timing.
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, m, w, q, k, v, dev, flush)
+
+    result = None
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            dt, desc, cores = cpu_sample(w, m, q, k, v, args.baseline_slices)
+            val, _full = cpu_baseline_value(w, dt, args.baseline_slices)
+            cpu = {"value": val, "unit": "tokens/s", "cores": cores, "kind": "port",
+                   "sample": desc, "sample_seconds": round(dt, 3)}
+        launches_per_step = 4  # k_hash_keys, k_bucket_trim, k_select_merge, k_attn_fwd
+        result = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
+            "data": "synthetic (seeded N(0,1) activations; random-init weights in reference order)",
+            "config": {"workload": w.name, "B": w.B, "N": w.N, "M": w.M, "H": w.H, "n_kv": w.n_kv,
+                       "d_head": w.d, "K": w.K, "window": w.window, "R": w.R, "probes": w.T,
+                       "causal": w.causal, "cross": w.cross,
+                       "parallelism": f"weak: one full batch per GPU x{world}",
+                       "l2": "flushed (256 MB write) between timed steps"},
+            "roofline": {"kernel": "k_attn_fwd", "bound": "hbm", "achieved": attn_gbs, "peak": peak,
+                         "unit": "GB/s", "frac": attn_gbs / peak, "traffic": traffic,
+                         "peak_source": f"{peak_src} hbm_gbs",
+                         "algorithmic_bytes": alg_bytes},
+            "step_roofline": {"achieved": step_gbs, "frac": step_gbs / peak, "unit": "GB/s",
+                              "note": "attention algorithmic bytes over graph build + attention"},
+            "kernels_ms": {"graph_build": ms_graph, "attention": ms_attn},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(result))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def run_e2e(args, m, w, q, k, v, dev, flush):
+    import torch
+    qh = q.transpose(1, 2).contiguous().cpu().pin_memory()      # (B, N, H, d)
+    kh = k.transpose(1, 2).contiguous().cpu().pin_memory()      # (B, M, n_kv, d)
+    vh = v.transpose(1, 2).contiguous().cpu().pin_memory()
+    qd, kd, vd = torch.empty_like(qh, device=dev), torch.empty_like(kh, device=dev), torch.empty_like(vh, device=dev)
+    outh = torch.empty((w.B, w.H, w.N, w.d), dtype=q.dtype).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+    causal = w.causal and not w.cross
+
+    def one():
+        qd.copy_(qh, non_blocking=True)
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
+        q4, k4, v4 = qd.transpose(1, 2), kd.transpose(1, 2), vd.transpose(1, 2)
+        nb, valid = m.build_graph(q4, k4, w.N, w.M, w.B, dev, causal, w.cross)
+        out = m.apply_graph(q4, k4, v4, nb, valid)
+        outh.copy_(out, non_blocking=True)
+
+    with torch.no_grad():
+        for _ in range(max(1, args.warmup)):
+            one()
+        torch.cuda.synchronize()
+        evs = []
+        for _ in range(args.steps):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            one()
+            b.record(stream)
+            evs.append((a, b))
+        torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    h2d = (qh.numel() + kh.numel() + vh.numel()) * qh.element_size()
+    d2h = outh.numel() * outh.element_size()
+    return {"value": w.B * w.N / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "api": "SparseAttention.build_graph + apply_graph (int64/bool graph contract)"}
+
+
+# ---------------------------------------------------------------------------
+# Reference arm: the CPU restatement (oracle port) on the host cores
+# ---------------------------------------------------------------------------
+def run_reference(args):
+    world, rank, local = dist_info()
+    if rank != 0:
+        return None
+    import torch
+    from ssa_b200.workloads import WORKLOADS, make_module, make_x, project
+
+    w = WORKLOADS[args.workload]
+    torch.set_num_threads(os.cpu_count() or 1)
+    m = make_module(w, "cpu")
+    slices = args.baseline_slices
+    ng = min(slices, w.n_kv)                 # kv groups in the sample (batch row 0)
+    rep = w.H // w.n_kv
+    x, kv = make_x(w, "cpu", seed=1, batch=1)
+    src = kv if kv is not None else x
+    with torch.no_grad():                     # project only the sampled heads' columns
+        def proj(lin, rows_, inp, heads):
+            y = inp.float() @ lin.weight[:rows_].float().T
+            return y.to(w.torch_dtype).view(1, inp.shape[1], heads, w.d).transpose(1, 2)
+        q = proj(m.Wq, ng * rep * w.d, x, ng * rep)
+        k = proj(m.Wk, ng * w.d, src, ng)
+        v = proj(m.Wv, ng * w.d, src, ng)
+    del x, kv, src
+    w1 = type(w)(**{**w.__dict__, "B": 1, "H": ng * rep, "n_kv": ng,
+                    "d_model": ng * rep * w.d})
+    slices = min(slices, ng)
+    for _ in range(max(0, min(args.warmup, 1))):
+        cpu_sample(w1, m, q, k, v, 1)
+    times = []
+    desc, cores = "", 1
+    for _ in range(args.steps):
+        dt, desc, cores = cpu_sample(w1, m, q, k, v, slices)
+        times.append(dt)
+    dt = statistics.mean(times)
+    full = dt * (w.B * w.n_kv) / slices
+    value = w.B * w.N / full
+    desc = desc.replace(f"{slices} of {w1.B * w1.n_kv}", f"{slices} of {w.B * w.n_kv}")
+    res = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+           "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": full * 1e3,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
+           "data": "synthetic", "config": {"workload": w.name, "B": w.B, "N": w.N, "H": w.H,
+                                           "n_kv": w.n_kv, "K": w.K},
+           "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                            "sample": desc},
+           "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(res))
+    return res
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,176 @@
+/*
+ * ssa_b200.h -- C ABI of the B200 (sm_100a) sparse-attention hot path.
+ *
+ * A drop-in for the hot path of daedalus/SSA's `sparse_attention.py`: the
+ * LSH neighbor-graph build (hash, bucket, multi-probe, rescore + top-k,
+ * window/global/self merge) and gather attention, forward and backward.
+ *
+ * Conventions
+ *   - Every pointer argument is DEVICE memory unless stated otherwise; the
+ *     caller owns every buffer (including the workspace). No entry point
+ *     allocates memory or synchronises the stream.
+ *   - `stream` is a cudaStream_t passed as void*. Work is enqueued on it.
+ *   - Tensors are described by a base pointer and element strides; the last
+ *     (head-dim) axis must be contiguous. Query-side tensors are (B, H, N, d);
+ *     key/value tensors are (B, n_kv, M, d) and head h reads kv head
+ *     h / (H / n_kv) -- the reference materialises that mapping with
+ *     repeat_interleave (sparse_attention.py:1305-1315); here it is an index.
+ *   - dtype: SSA_F32 or SSA_BF16 for q/k/v/out. Index outputs are int32.
+ *   - Every function returns an ssa_status; 0 is success.
+ */
+#ifndef SSA_B200_H_
+#define SSA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SSA_API __attribute__((visibility("default")))
+#else
+#define SSA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  SSA_OK = 0,
+  SSA_ERR_INVALID = 1,      /* bad shape, stride, pointer or parameter */
+  SSA_ERR_UNSUPPORTED = 2,  /* valid for the reference, not built here (message says why) */
+  SSA_ERR_WORKSPACE = 3,    /* workspace missing or too small */
+  SSA_ERR_CUDA = 4,         /* a CUDA launch or API call failed */
+  SSA_ERR_DEVICE = 5        /* a kernel raised its device error flag */
+} ssa_status;
+
+typedef enum { SSA_F32 = 0, SSA_BF16 = 1 } ssa_dtype;
+
+/* Geometry and hyper-parameters of one graph build. The derived values
+ * (C, p_eff, A) are passed in so the caller controls them exactly as the
+ * reference derives them: C = 4 * lsh_k (:1294), p_eff =
+ * clamp(round(log2(M / C)), 1, max_num_hashes) (:552-557), A = min(lsh_k,
+ * R * C * (1 + min(T, p_eff))) (:898). */
+typedef struct {
+  int32_t B, H, n_kv, N, M, d;
+  int32_t dtype;            /* ssa_dtype of q and k */
+  int32_t R;                /* num_hash_rounds */
+  int32_t max_p;            /* max_num_hashes: planes per round in rand_proj */
+  int32_t p_eff;            /* planes used this call (1..12) */
+  int32_t C;                /* candidates kept per bucket (lsh_candidates) */
+  int32_t T;                /* lsh_num_probes (clamped to p_eff inside) */
+  int32_t A;                /* LSH output width (top-k) */
+  int32_t causal;           /* 1: causal LSH + window */
+  int32_t is_cross;         /* 1: cross-attention (no window, no self slot) */
+  int32_t K;                /* num_neighbors */
+  int32_t window;           /* window_size (half width) */
+  int32_t G;                /* number of global key indices */
+  int64_t q_sb, q_sh, q_sn; /* element strides of q (B, H, N, d) */
+  int64_t k_sb, k_sh, k_sm; /* element strides of k (B, n_kv, M, d) */
+} ssa_graph_params;
+
+/* Neighbor-slot width of the merged graph: self + min(K-1, Kall) slots for
+ * self-attention, min(K, Kall) for cross-attention, Kall = window slots +
+ * G + A (merge_neighbors, sparse_attention.py:1071-1076). */
+SSA_API int32_t ssa_graph_width(const ssa_graph_params* p);
+
+/* Bytes of device workspace ssa_build_graph / ssa_lsh_select need. */
+SSA_API size_t ssa_graph_workspace_size(const ssa_graph_params* p);
+
+/*
+ * SparseAttention.build_graph (sparse_attention.py:1325-1390): window +
+ * global + LSH + self graph, merged and deduplicated.
+ *   q          (B,H,N,d) per q_s* strides;  k (B,n_kv,M,d) per k_s* strides
+ *   rand_proj  (R, max_p, d) fp32 contiguous: the LSHGraphBuilder hyperplanes
+ *   glob       (G,) int32: global key indices, already clamped to [0, M-1]
+ *   nb_out     (B,H,N,W) int32, valid_out (B,H,N,W) uint8, W = ssa_graph_width
+ *   lsh_out    optional (B,H,N,A) int32: the LSH selection (any order)
+ */
+SSA_API int ssa_build_graph(const ssa_graph_params* p, const void* q, const void* k,
+                    const float* rand_proj, const int32_t* glob, int32_t* nb_out,
+                    uint8_t* valid_out, int32_t* lsh_out, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/*
+ * LSHGraphBuilder.forward (sparse_attention.py:814-959): per (b, h, query)
+ * the top-A distinct candidate keys by q.k over the union of R rounds x
+ * (1 + probes) buckets, with the reference's overflow, causal, empty-bucket
+ * and fallback rules. lsh_out (B,H,N,A) int32 in descending score order,
+ * fallback slots last (the reference's topk order).
+ */
+SSA_API int ssa_lsh_select(const ssa_graph_params* p, const void* q, const void* k,
+                   const float* rand_proj, const int32_t* glob, int32_t* lsh_out,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * merge_neighbors (sparse_attention.py:966-1089) over explicit sources:
+ *   lsh      (B,H,N,A) int32    win (N,Kw) int32 (Kw may be 0)
+ *   glob     (G,) int32         self_idx (B,H,N) int32, NULL for cross-attention
+ *   true_max device int32 scalar: the maximum over win, glob and lsh (the
+ *            reference's true_max_idx, :1031)
+ * Output (B,H,N,W): W = min(K-1, Kw+G+A) + 1 with self, min(K, Kw+G+A)
+ * without. Uses p->B, H, N, A, K, G.
+ */
+SSA_API int ssa_merge(const ssa_graph_params* p, const int32_t* lsh, const int32_t* glob,
+                      const int32_t* win, int32_t Kw, const int32_t* self_idx,
+                      const int32_t* true_max, int32_t* nb_out, uint8_t* valid_out,
+                      void* stream);
+
+/*
+ * Per-round bucket ids, sign(x . plane_j) packed LSB-first: the reference's
+ * _hash (sparse_attention.py:559-591). x (B, heads, rows, d) with strides;
+ * ids_out (B*heads, R, rows) int32.
+ */
+SSA_API int ssa_hash_ids(const void* x, int32_t dtype, int32_t B, int32_t heads, int32_t rows,
+                 int32_t d, int64_t sb, int64_t sh, int64_t sn, const float* rand_proj,
+                 int32_t R, int32_t max_p, int32_t p_eff, int32_t* ids_out, void* stream);
+
+/* Geometry of gather attention. */
+typedef struct {
+  int32_t B, H, n_kv, N, M, d;
+  int32_t Kn;               /* neighbor slots per query */
+  int32_t dtype;            /* ssa_dtype of q, k, v, out (and dO, dq, dk, dv) */
+  int32_t nb_i64;           /* 1: neighbors are int64 (reference dtype), else int32 */
+  int32_t fp32_weights;     /* SSAConfig.fp32_attn_weights */
+  float scale;              /* d ** -0.5 (sparse_attention.py:1249) */
+  int64_t q_sb, q_sh, q_sn; /* (B,H,N,d) */
+  int64_t k_sb, k_sh, k_sm; /* (B,n_kv,M,d) */
+  int64_t v_sb, v_sh, v_sm; /* (B,n_kv,M,d) */
+  int64_t o_sb, o_sh, o_sn; /* out / dO / dq (B,H,N,d) */
+} ssa_attn_params;
+
+/*
+ * sparse_gather_attention forward (sparse_attention.py:1096-1199) as called
+ * by SparseAttention.apply_graph (:1392-1418): fp32 scores q.k * scale over
+ * the Kn gathered keys, invalid slots masked, fp32 softmax, weights cast to
+ * the value dtype (or kept fp32 with fp32_weights), weighted sum of values.
+ *   nb (B,H,N,Kn) int32/int64 contiguous, valid (B,H,N,Kn) uint8/bool
+ *   out (B,H,N,d) per o_s* strides; lse (B,H,N) fp32, optional (backward)
+ */
+SSA_API int ssa_attn_fwd(const ssa_attn_params* p, const void* q, const void* k, const void* v,
+                 const void* nb, const uint8_t* valid, void* out, float* lse,
+                 void* stream);
+
+/*
+ * Backward of ssa_attn_fwd (the autograd graph of :1147-1198): dq, and dk/dv
+ * accumulated per kv head over every (head, query, slot) edge that gathered
+ * that key -- the index_add / repeat_interleave backward -- as a segmented
+ * reduction over the inverted neighbor index (no floating-point atomics; the
+ * result is deterministic). dO/dq share the o_s* strides; dk/dv are
+ * (B,n_kv,M,d) contiguous. Needs ssa_attn_bwd_workspace_size bytes.
+ */
+SSA_API size_t ssa_attn_bwd_workspace_size(const ssa_attn_params* p);
+SSA_API int ssa_attn_bwd(const ssa_attn_params* p, const void* q, const void* k, const void* v,
+                 const void* nb, const uint8_t* valid, const void* dO, const float* lse,
+                 void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+/* Human-readable text for the last error on this host thread. */
+SSA_API const char* ssa_last_error(void);
+
+/* ABI version of this library (major * 100 + minor). */
+SSA_API int32_t ssa_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SSA_B200_H_ */

@@ -1,0 +1,423 @@
+// ssa_attn.cu -- gather attention over a neighbor graph, forward and backward.
+//
+// Forward replaces sparse_gather_attention (sparse_attention.py:1096-1199):
+// for every (b, h, query) row, scores s_j = (q . k[nb_j]) * scale in fp32 over
+// the Kn neighbor slots, invalid slots -> -inf, fp32 softmax, the weights cast
+// to the value dtype (or kept fp32 with fp32_weights), weighted sum of v rows.
+//
+// One warp owns one row. The warp is split into four 8-lane groups; a group
+// gathers one neighbor row per step, each lane moving a contiguous 32-byte
+// slice (16 bf16 or 8 fp32 of a 128-wide head), so one warp instruction
+// touches four full rows. Scores stay in shared memory (K <= a few hundred),
+// which allows the exact two-pass softmax the reference computes. Rows are
+// enumerated (b, kv-head, query, head-in-group) so that the heads sharing a
+// kv head, and consecutive queries, run close together and re-hit L2/L1 for
+// the shared window/global rows; the (b, kv-head) slices stream through L2
+// one after another.
+//
+// Backward: per row, dq and the per-edge weights (value weight p, and
+// scale * dS); then the edges are radix-sorted by (kv slice, key) -- a stable
+// sort, so within a key edges keep their row order -- and one warp per key
+// sums its segment in that order into dk/dv. No floating-point atomics: the
+// result is bitwise reproducible.
+#include <cub/device/device_radix_sort.cuh>
+
+#include "ssa_common.cuh"
+#include "ssa_internal.h"
+
+namespace ssa {
+
+__device__ __forceinline__ void decode_row(const AttnDev& a, int64_t i, int& b, int& h, int& n,
+                                           int& g) {
+  const int hh = (int)(i % a.rep);
+  int64_t t = i / a.rep;
+  n = (int)(t % a.N);
+  t /= a.N;
+  g = (int)(t % a.n_kv);
+  b = (int)(t / a.n_kv);
+  h = g * a.rep + hh;
+}
+
+template <typename IT>
+__device__ __forceinline__ int load_nb(const void* nb, int64_t i) {
+  return (int)__ldg(static_cast<const IT*>(nb) + i);
+}
+
+// A slot takes part only if it is valid and its index lies in [0, M): an
+// out-of-range index (possible only from a caller-built graph) is treated as
+// padding instead of being dereferenced.
+template <typename IT>
+__device__ __forceinline__ bool slot_ok(const AttnDev& a, const void* nbr, const uint8_t* vr, int j) {
+  if (!__ldg(vr + j)) return false;
+  const int64_t key = (int64_t)__ldg(static_cast<const IT*>(nbr) + j);
+  return key >= 0 && key < a.M;
+}
+
+template <int DT, int EPL>
+__device__ __forceinline__ void load_slice(const void* row, int e0, int d, float* o) {
+#pragma unroll
+  for (int c = 0; c < EPL; c += 4) {
+    if (e0 + c < d) {
+      const float4 x = load4<DT>(row, e0 + c);
+      o[c] = x.x; o[c + 1] = x.y; o[c + 2] = x.z; o[c + 3] = x.w;
+    } else {
+      o[c] = o[c + 1] = o[c + 2] = o[c + 3] = 0.f;
+    }
+  }
+}
+
+template <int DT, int EPL, bool FP32W, typename IT>
+__global__ void __launch_bounds__(256) k_attn_fwd(AttnDev a) {
+  extern __shared__ __align__(16) float s_all[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t i = (int64_t)blockIdx.x * 8 + warp;
+  if (i >= (int64_t)a.B * a.H * a.N) return;
+  int b, h, n, g;
+  decode_row(a, i, b, h, n, g);
+  const int Kp = (a.Kn + 31) & ~31;
+  float* s = s_all + warp * Kp;
+  const int grp = lane >> 3, li = lane & 7, e0 = li * EPL;
+  const int64_t row = ((int64_t)b * a.H + h) * a.N + n;
+  const void* nbr = static_cast<const char*>(a.nb) + row * a.Kn * (int64_t)sizeof(IT);
+  const uint8_t* vr = a.valid + row * a.Kn;
+  const void* kb = row_ptr<DT>(a.k, b * a.k_sb + g * a.k_sh);
+  const void* vb = row_ptr<DT>(a.v, b * a.v_sb + g * a.v_sh);
+
+  float qv[EPL];
+  load_slice<DT, EPL>(row_ptr<DT>(a.q, b * a.q_sb + h * a.q_sh + (int64_t)n * a.q_sn), e0, a.d, qv);
+
+  const int iters = (a.Kn + 3) >> 2;
+  // Pass 1: scores.
+  for (int it = 0; it < iters; it += 2) {
+    float part[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int j = (it + u) * 4 + grp;
+      part[u] = 0.f;
+      if (it + u < iters && j < a.Kn && slot_ok<IT>(a, nbr, vr, j)) {
+        const int key = load_nb<IT>(nbr, j);
+        float kv[EPL];
+        load_slice<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), e0, a.d, kv);
+        float acc = 0.f;
+#pragma unroll
+        for (int c = 0; c < EPL; ++c) acc = fmaf(qv[c], kv[c], acc);
+        part[u] = acc;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      float x = part[u];
+      x += __shfl_xor_sync(0xffffffffu, x, 1);
+      x += __shfl_xor_sync(0xffffffffu, x, 2);
+      x += __shfl_xor_sync(0xffffffffu, x, 4);
+      const int j = (it + u) * 4 + grp;
+      if (li == 0 && it + u < iters && j < a.Kn)
+        s[j] = slot_ok<IT>(a, nbr, vr, j) ? x * a.scale : -INFINITY;
+    }
+  }
+  __syncwarp();
+  // Softmax in fp32 (:1167).
+  float mx = -INFINITY;
+  for (int j = lane; j < a.Kn; j += 32) mx = fmaxf(mx, s[j]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.f;
+  for (int j = lane; j < a.Kn; j += 32) sum += expf(s[j] - mx);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  for (int j = lane; j < a.Kn; j += 32) {
+    float p = expf(s[j] - mx) / sum;
+    if (DT == kDtBF16 && !FP32W) p = round_bf16(p);  // attn.to(v.dtype) (:1190)
+    s[j] = p;
+  }
+  __syncwarp();
+  // Pass 2: weighted sum of value rows.
+  float acc[EPL];
+#pragma unroll
+  for (int c = 0; c < EPL; ++c) acc[c] = 0.f;
+  for (int it = 0; it < iters; it += 2) {
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int j = (it + u) * 4 + grp;
+      if (it + u < iters && j < a.Kn && slot_ok<IT>(a, nbr, vr, j)) {
+        const int key = load_nb<IT>(nbr, j);
+        const float p = s[j];
+        float vv[EPL];
+        load_slice<DT, EPL>(row_ptr<DT>(vb, (int64_t)key * a.v_sm), e0, a.d, vv);
+#pragma unroll
+        for (int c = 0; c < EPL; ++c) acc[c] = fmaf(p, vv[c], acc[c]);
+      }
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < EPL; ++c) {
+    acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], 8);
+    acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], 16);
+  }
+  if (grp == 0) {
+    void* orow = row_ptr_mut<DT>(a.out, b * a.o_sb + h * a.o_sh + (int64_t)n * a.o_sn);
+#pragma unroll
+    for (int c = 0; c < EPL; ++c)
+      if (e0 + c < a.d) store1<DT>(orow, e0 + c, acc[c]);
+  }
+  if (a.lse && lane == 0) a.lse[row] = mx + logf(sum);
+}
+
+// ---------------------------------------------------------------------------
+// Backward, stage 1: per row -- dq, edge weights, edge keys.
+// ---------------------------------------------------------------------------
+template <int DT, int EPL, bool FP32W, typename IT>
+__global__ void __launch_bounds__(256) k_attn_bwd_rows(AttnDev a) {
+  extern __shared__ __align__(16) float s_all[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t i = (int64_t)blockIdx.x * 8 + warp;
+  if (i >= (int64_t)a.B * a.H * a.N) return;
+  int b, h, n, g;
+  decode_row(a, i, b, h, n, g);
+  const int Kp = (a.Kn + 31) & ~31;
+  float* sp = s_all + warp * 2 * Kp;  // p_j
+  float* sdp = sp + Kp;               // dP_j
+  const int grp = lane >> 3, li = lane & 7, e0 = li * EPL;
+  const int64_t row = ((int64_t)b * a.H + h) * a.N + n;
+  const void* nbr = static_cast<const char*>(a.nb) + row * a.Kn * (int64_t)sizeof(IT);
+  const uint8_t* vr = a.valid + row * a.Kn;
+  const void* kb = row_ptr<DT>(a.k, b * a.k_sb + g * a.k_sh);
+  const void* vb = row_ptr<DT>(a.v, b * a.v_sb + g * a.v_sh);
+  const int64_t orow_off = b * a.o_sb + h * a.o_sh + (int64_t)n * a.o_sn;
+
+  float qv[EPL], gv[EPL];
+  load_slice<DT, EPL>(row_ptr<DT>(a.q, b * a.q_sb + h * a.q_sh + (int64_t)n * a.q_sn), e0, a.d, qv);
+  load_slice<DT, EPL>(row_ptr<DT>(a.dO, orow_off), e0, a.d, gv);
+  const float lse = a.lse_in[row];
+  const int iters = (a.Kn + 3) >> 2;
+  for (int it = 0; it < iters; ++it) {
+    const int j = it * 4 + grp;
+    float ps = 0.f, pd = 0.f;
+    const bool ok = j < a.Kn && slot_ok<IT>(a, nbr, vr, j);
+    if (ok) {
+      const int key = load_nb<IT>(nbr, j);
+      float kv[EPL], vv[EPL];
+      load_slice<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), e0, a.d, kv);
+      load_slice<DT, EPL>(row_ptr<DT>(vb, (int64_t)key * a.v_sm), e0, a.d, vv);
+#pragma unroll
+      for (int c = 0; c < EPL; ++c) {
+        ps = fmaf(qv[c], kv[c], ps);
+        pd = fmaf(gv[c], vv[c], pd);
+      }
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      pd += __shfl_xor_sync(0xffffffffu, pd, o);
+    }
+    if (li == 0 && j < a.Kn) {
+      sp[j] = ok ? expf(ps * a.scale - lse) : 0.f;
+      sdp[j] = ok ? pd : 0.f;
+    }
+  }
+  __syncwarp();
+  float dsum = 0.f;
+  for (int j = lane; j < a.Kn; j += 32) dsum = fmaf(sp[j], sdp[j], dsum);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, o);
+  const uint32_t BGM = (uint32_t)(a.B * a.n_kv) * (uint32_t)a.M;
+  const uint32_t bgM = (uint32_t)(b * a.n_kv + g) * (uint32_t)a.M;
+  for (int j = lane; j < a.Kn; j += 32) {
+    const float p = sp[j];
+    const float ds = p * (sdp[j] - dsum) * a.scale;
+    const int64_t e = row * a.Kn + j;
+    const bool ok = slot_ok<IT>(a, nbr, vr, j);
+    a.ep[e] = (DT == kDtBF16 && !FP32W) ? round_bf16(p) : p;
+    a.eds[e] = ds;
+    a.ekey[e] = ok ? bgM + (uint32_t)load_nb<IT>(nbr, j) : BGM;
+    a.eid[e] = (uint32_t)e;
+    sdp[j] = ds;
+  }
+  __syncwarp();
+  float acc[EPL];
+#pragma unroll
+  for (int c = 0; c < EPL; ++c) acc[c] = 0.f;
+  for (int it = 0; it < iters; ++it) {
+    const int j = it * 4 + grp;
+    if (j < a.Kn && slot_ok<IT>(a, nbr, vr, j)) {
+      const int key = load_nb<IT>(nbr, j);
+      const float ds = sdp[j];
+      float kv[EPL];
+      load_slice<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), e0, a.d, kv);
+#pragma unroll
+      for (int c = 0; c < EPL; ++c) acc[c] = fmaf(ds, kv[c], acc[c]);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < EPL; ++c) {
+    acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], 8);
+    acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], 16);
+  }
+  if (grp == 0) {
+    void* dqr = row_ptr_mut<DT>(a.dq, orow_off);
+#pragma unroll
+    for (int c = 0; c < EPL; ++c)
+      if (e0 + c < a.d) store1<DT>(dqr, e0 + c, acc[c]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward, stage 3: one warp per (kv slice, key) sums its sorted segment.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int64_t lower_bound_u32(const uint32_t* a, int64_t n, uint32_t x) {
+  int64_t lo = 0, hi = n;
+  while (lo < hi) {
+    const int64_t mid = (lo + hi) >> 1;
+    if (__ldg(a + mid) < x) lo = mid + 1; else hi = mid;
+  }
+  return lo;
+}
+
+template <int DT, int EPW>
+__global__ void __launch_bounds__(256) k_dkdv(AttnDev a, int64_t n_edges) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t key = (int64_t)blockIdx.x * 8 + warp;  // bg * M + m
+  const int64_t total = (int64_t)a.B * a.n_kv * a.M;
+  if (key >= total) return;
+  const int64_t lo = lower_bound_u32(a.skey, n_edges, (uint32_t)key);
+  const int64_t hi = lower_bound_u32(a.skey, n_edges, (uint32_t)key + 1u);
+  float dk[EPW], dv[EPW];
+#pragma unroll
+  for (int c = 0; c < EPW; ++c) dk[c] = dv[c] = 0.f;
+  const int e0 = lane * EPW;
+  for (int64_t s = lo; s < hi; ++s) {
+    const uint32_t e = __ldg(a.sid + s);
+    const int64_t row = e / (uint32_t)a.Kn;
+    const int n = (int)(row % a.N);
+    const int64_t bh = row / a.N;
+    const int h = (int)(bh % a.H), b = (int)(bh / a.H);
+    const float p = __ldg(a.ep + e), ds = __ldg(a.eds + e);
+    const void* qr = row_ptr<DT>(a.q, b * a.q_sb + h * a.q_sh + (int64_t)n * a.q_sn);
+    const void* gr = row_ptr<DT>(a.dO, b * a.o_sb + h * a.o_sh + (int64_t)n * a.o_sn);
+#pragma unroll
+    for (int c = 0; c < EPW; ++c) {
+      if (e0 + c < a.d) {
+        dk[c] = fmaf(ds, load1<DT>(qr, e0 + c), dk[c]);
+        dv[c] = fmaf(p, load1<DT>(gr, e0 + c), dv[c]);
+      }
+    }
+  }
+  void* dkr = row_ptr_mut<DT>(a.dk, key * a.d);
+  void* dvr = row_ptr_mut<DT>(a.dv, key * a.d);
+#pragma unroll
+  for (int c = 0; c < EPW; ++c) {
+    if (e0 + c < a.d) {
+      store1<DT>(dkr, e0 + c, dk[c]);
+      store1<DT>(dvr, e0 + c, dv[c]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host launchers
+// ---------------------------------------------------------------------------
+template <int DT, int EPL, bool FP32W, typename IT>
+static cudaError_t fwd_t(const AttnDev& a, cudaStream_t st) {
+  const int Kp = (a.Kn + 31) & ~31;
+  const size_t smem = (size_t)8 * Kp * sizeof(float);
+  auto fn = k_attn_fwd<DT, EPL, FP32W, IT>;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int64_t rows = (int64_t)a.B * a.H * a.N;
+  fn<<<(unsigned)((rows + 7) / 8), 256, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <int DT, int EPL>
+static cudaError_t fwd_e(const AttnDev& a, cudaStream_t st) {
+  if (a.fp32w) return a.nb_i64 ? fwd_t<DT, EPL, true, int64_t>(a, st) : fwd_t<DT, EPL, true, int32_t>(a, st);
+  return a.nb_i64 ? fwd_t<DT, EPL, false, int64_t>(a, st) : fwd_t<DT, EPL, false, int32_t>(a, st);
+}
+
+template <int DT>
+static cudaError_t fwd_d(const AttnDev& a, cudaStream_t st) {
+  if (a.d <= 32) return fwd_e<DT, 4>(a, st);
+  if (a.d <= 64) return fwd_e<DT, 8>(a, st);
+  if (a.d <= 128) return fwd_e<DT, 16>(a, st);
+  return fwd_e<DT, 32>(a, st);
+}
+
+cudaError_t launch_attn_fwd(const AttnDev& a, cudaStream_t st) {
+  return a.dtype == kDtF32 ? fwd_d<kDtF32>(a, st) : fwd_d<kDtBF16>(a, st);
+}
+
+size_t attn_bwd_workspace_layout(const AttnDev& a, AttnDev* out, void* ws) {
+  const int64_t E = (int64_t)a.B * a.H * a.N * a.Kn;
+  size_t tmp = 0;
+  cub::DeviceRadixSort::SortPairs(nullptr, tmp, (const uint32_t*)nullptr, (uint32_t*)nullptr,
+                                  (const uint32_t*)nullptr, (uint32_t*)nullptr, (int)E, 0, 32);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = (off + bytes + 255) & ~size_t(255);
+    return o;
+  };
+  const size_t o_ep = take(4 * E), o_eds = take(4 * E), o_ekey = take(4 * E), o_eid = take(4 * E);
+  const size_t o_skey = take(4 * E), o_sid = take(4 * E), o_tmp = take(tmp);
+  if (out) {
+    char* base = static_cast<char*>(ws);
+    out->ep = reinterpret_cast<float*>(base + o_ep);
+    out->eds = reinterpret_cast<float*>(base + o_eds);
+    out->ekey = reinterpret_cast<uint32_t*>(base + o_ekey);
+    out->eid = reinterpret_cast<uint32_t*>(base + o_eid);
+    out->skey = reinterpret_cast<uint32_t*>(base + o_skey);
+    out->sid = reinterpret_cast<uint32_t*>(base + o_sid);
+    out->sort_tmp = base + o_tmp;
+    out->sort_tmp_bytes = tmp;
+  }
+  return off;
+}
+
+template <int DT, int EPL, bool FP32W, typename IT>
+static cudaError_t bwd_rows_t(const AttnDev& a, cudaStream_t st) {
+  const int Kp = (a.Kn + 31) & ~31;
+  const size_t smem = (size_t)8 * 2 * Kp * sizeof(float);
+  auto fn = k_attn_bwd_rows<DT, EPL, FP32W, IT>;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int64_t rows = (int64_t)a.B * a.H * a.N;
+  fn<<<(unsigned)((rows + 7) / 8), 256, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <int DT, int EPL>
+static cudaError_t bwd_rows_e(const AttnDev& a, cudaStream_t st) {
+  if (a.fp32w) return a.nb_i64 ? bwd_rows_t<DT, EPL, true, int64_t>(a, st) : bwd_rows_t<DT, EPL, true, int32_t>(a, st);
+  return a.nb_i64 ? bwd_rows_t<DT, EPL, false, int64_t>(a, st) : bwd_rows_t<DT, EPL, false, int32_t>(a, st);
+}
+
+template <int DT>
+static cudaError_t bwd_d(const AttnDev& a, cudaStream_t st) {
+  cudaError_t e;
+  if (a.d <= 32) e = bwd_rows_e<DT, 4>(a, st);
+  else if (a.d <= 64) e = bwd_rows_e<DT, 8>(a, st);
+  else if (a.d <= 128) e = bwd_rows_e<DT, 16>(a, st);
+  else e = bwd_rows_e<DT, 32>(a, st);
+  if (e != cudaSuccess) return e;
+  const int64_t E = (int64_t)a.B * a.H * a.N * a.Kn;
+  const uint64_t maxkey = (uint64_t)a.B * a.n_kv * a.M;
+  int end_bit = 1;
+  while ((1ull << end_bit) <= maxkey) ++end_bit;
+  size_t tmp = a.sort_tmp_bytes;
+  e = cub::DeviceRadixSort::SortPairs(a.sort_tmp, tmp, a.ekey, a.skey, a.eid, a.sid, (int)E, 0,
+                                      end_bit, st);
+  if (e != cudaSuccess) return e;
+  const int64_t keys = (int64_t)a.B * a.n_kv * a.M;
+  const unsigned grid = (unsigned)((keys + 7) / 8);
+  if (a.d <= 32) k_dkdv<DT, 1><<<grid, 256, 0, st>>>(a, E);
+  else if (a.d <= 64) k_dkdv<DT, 2><<<grid, 256, 0, st>>>(a, E);
+  else if (a.d <= 128) k_dkdv<DT, 4><<<grid, 256, 0, st>>>(a, E);
+  else k_dkdv<DT, 8><<<grid, 256, 0, st>>>(a, E);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attn_bwd(const AttnDev& a, cudaStream_t st) {
+  return a.dtype == kDtF32 ? bwd_d<kDtF32>(a, st) : bwd_d<kDtBF16>(a, st);
+}
+
+}  // namespace ssa

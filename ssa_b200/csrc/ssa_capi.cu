@@ -1,0 +1,283 @@
+// ssa_capi.cu -- the extern "C" entry points declared in include/ssa_b200.h.
+//
+// Validates shapes, strides and alignment, carves the caller's workspace,
+// and enqueues the kernels on the caller's stream. Nothing here allocates,
+// synchronises or touches host-side tensors.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "../../include/ssa_b200.h"
+#include "ssa_common.cuh"
+#include "ssa_internal.h"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(SSA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int elem_align(int dtype) { return dtype == SSA_F32 ? 16 : 8; }
+
+int check_rows(const char* name, const void* ptr, int dtype, int d, int64_t s0, int64_t s1,
+               int64_t s2) {
+  if (!ptr) return fail(SSA_ERR_INVALID, "%s is NULL", name);
+  if (!aligned(ptr, elem_align(dtype)))
+    return fail(SSA_ERR_UNSUPPORTED, "%s must be %d-byte aligned", name, elem_align(dtype));
+  if (d % 4) return fail(SSA_ERR_UNSUPPORTED, "head dim d=%d must be a multiple of 4", d);
+  if ((s0 % 4) || (s1 % 4) || (s2 % 4))
+    return fail(SSA_ERR_UNSUPPORTED, "%s strides (%lld,%lld,%lld) must be multiples of 4 elements",
+                name, (long long)s0, (long long)s1, (long long)s2);
+  if (s0 < 0 || s1 < 0 || s2 < 0) return fail(SSA_ERR_INVALID, "%s has a negative stride", name);
+  return SSA_OK;
+}
+
+int32_t graph_width(const ssa_graph_params* p) {
+  const int kw = p->is_cross ? 0 : 2 * p->window + 1;
+  const int kall = kw + p->G + p->A;
+  if (p->is_cross) return p->K < kall ? p->K : kall;
+  return (p->K - 1 < kall ? p->K - 1 : kall) + 1;
+}
+
+int check_graph(const ssa_graph_params* p) {
+  if (!p) return fail(SSA_ERR_INVALID, "params is NULL");
+  if (p->B < 1 || p->H < 1 || p->n_kv < 1 || p->N < 1 || p->M < 1 || p->d < 1)
+    return fail(SSA_ERR_INVALID, "B,H,n_kv,N,M,d must be >= 1");
+  if (p->H % p->n_kv)
+    return fail(SSA_ERR_INVALID, "num_heads (%d) must be divisible by num_kv_heads (%d)", p->H, p->n_kv);
+  if (p->dtype != SSA_F32 && p->dtype != SSA_BF16) return fail(SSA_ERR_INVALID, "dtype must be F32 or BF16");
+  if (p->d > 128) return fail(SSA_ERR_UNSUPPORTED, "graph build supports head dim <= 128 (got %d)", p->d);
+  if (p->R < 1 || p->R > 64) return fail(SSA_ERR_INVALID, "num_hash_rounds must be in [1, 64]");
+  if (p->max_p < 1 || p->max_p > 12)
+    return fail(SSA_ERR_INVALID, "max_num_hashes must be in [1, 12] (reference asserts <= 12)");
+  if (p->p_eff < 1 || p->p_eff > p->max_p) return fail(SSA_ERR_INVALID, "p_eff must be in [1, max_num_hashes]");
+  if (p->C < 1 || p->A < 1 || p->T < 0 || p->K < 1 || p->window < 0 || p->G < 0)
+    return fail(SSA_ERR_INVALID, "C, A, K >= 1 and T, window, G >= 0 required");
+  if (p->M > (1 << 20)) return fail(SSA_ERR_UNSUPPORTED, "key length M=%d exceeds 2^20", p->M);
+  if (p->N > (1 << 30)) return fail(SSA_ERR_UNSUPPORTED, "query length too large");
+  if ((int64_t)p->B * p->H > 65535 || (int64_t)p->B * p->n_kv > 65535)
+    return fail(SSA_ERR_UNSUPPORTED, "B*H must be <= 65535");
+  if (p->is_cross && p->causal) return fail(SSA_ERR_INVALID, "cross-attention is never causal");
+  return SSA_OK;
+}
+
+ssa::GraphShape shape_of(const ssa_graph_params* p, bool need_lsh_scratch) {
+  ssa::GraphShape s;
+  s.B = p->B; s.H = p->H; s.n_kv = p->n_kv; s.N = p->N; s.M = p->M; s.d = p->d;
+  s.R = p->R; s.p = p->p_eff; s.A = p->A;
+  s.need_lsh_scratch = need_lsh_scratch;
+  return s;
+}
+
+ssa::GraphDev dev_of(const ssa_graph_params* p) {
+  ssa::GraphDev g;
+  memset(&g, 0, sizeof(g));
+  g.B = p->B; g.H = p->H; g.n_kv = p->n_kv; g.rep = p->H / p->n_kv; g.N = p->N; g.M = p->M;
+  g.d = p->d; g.dtype = p->dtype; g.R = p->R; g.max_p = p->max_p; g.p = p->p_eff; g.C = p->C;
+  g.Te = p->T < p->p_eff ? p->T : p->p_eff;
+  g.NT = g.R * (1 + g.Te);
+  g.NB = 1 << g.p;
+  g.W = (p->M + 63) / 64;
+  g.A = p->A; g.causal = p->causal; g.is_cross = p->is_cross; g.window = p->window; g.G = p->G;
+  g.Wout = graph_width(p);
+  g.q_sb = p->q_sb; g.q_sh = p->q_sh; g.q_sn = p->q_sn;
+  g.k_sb = p->k_sb; g.k_sh = p->k_sh; g.k_sm = p->k_sm;
+  return g;
+}
+
+int check_graph_inputs(const ssa_graph_params* p, const void* q, const void* k, const float* rp,
+                       const int32_t* glob) {
+  int rc;
+  if ((rc = check_rows("q", q, p->dtype, p->d, p->q_sb, p->q_sh, p->q_sn))) return rc;
+  if ((rc = check_rows("k", k, p->dtype, p->d, p->k_sb, p->k_sh, p->k_sm))) return rc;
+  if (!rp || !aligned(rp, 16)) return fail(SSA_ERR_INVALID, "rand_proj must be a 16-byte aligned fp32 array");
+  if (p->G > 0 && !glob) return fail(SSA_ERR_INVALID, "glob is NULL but G > 0");
+  return SSA_OK;
+}
+
+int check_select_fits(const ssa::GraphDev& g) {
+  int rows;
+  size_t smem;
+  if (ssa::choose_select_rows(g, &rows, &smem))
+    return fail(SSA_ERR_UNSUPPORTED,
+                "per-row top-k buffer does not fit in shared memory (A=%d, d=%d); reduce num_neighbors",
+                g.A, g.d);
+  return SSA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ssa_last_error(void) { return g_err; }
+
+int32_t ssa_abi_version(void) { return 100; }
+
+int32_t ssa_graph_width(const ssa_graph_params* p) { return p ? graph_width(p) : -1; }
+
+size_t ssa_graph_workspace_size(const ssa_graph_params* p) {
+  if (check_graph(p)) return 0;
+  return ssa::graph_workspace_layout(shape_of(p, false), nullptr);
+}
+
+static int run_graph(const ssa_graph_params* p, const void* q, const void* k, const float* rp,
+                     const int32_t* glob, int32_t* nb_out, uint8_t* valid_out, int32_t* lsh_out,
+                     void* ws, size_t ws_bytes, void* stream, int mode) {
+  int rc;
+  if ((rc = check_graph(p))) return rc;
+  if ((rc = check_graph_inputs(p, q, k, rp, glob))) return rc;
+  if (mode == 0 && (!nb_out || !valid_out)) return fail(SSA_ERR_INVALID, "nb_out/valid_out are NULL");
+  if (mode == 1 && !lsh_out) return fail(SSA_ERR_INVALID, "lsh_out is NULL");
+  const size_t need = ssa::graph_workspace_layout(shape_of(p, false), nullptr);
+  if (!ws || ws_bytes < need)
+    return fail(SSA_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, ws_bytes);
+  ssa::GraphDev g = dev_of(p);
+  g.ws = ws;
+  ssa::graph_workspace_layout(shape_of(p, false), &g);
+  g.q = q; g.k = k; g.rp = rp; g.glob = glob;
+  g.lsh = lsh_out; g.nb = nb_out; g.valid = valid_out;
+  if ((rc = check_select_fits(g))) return rc;
+  cudaError_t e = ssa::launch_graph(g, mode, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "graph build launch");
+  return SSA_OK;
+}
+
+int ssa_build_graph(const ssa_graph_params* p, const void* q, const void* k, const float* rand_proj,
+                    const int32_t* glob, int32_t* nb_out, uint8_t* valid_out, int32_t* lsh_out,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  return run_graph(p, q, k, rand_proj, glob, nb_out, valid_out, lsh_out, workspace,
+                   workspace_bytes, stream, 0);
+}
+
+int ssa_lsh_select(const ssa_graph_params* p, const void* q, const void* k, const float* rand_proj,
+                   const int32_t* glob, int32_t* lsh_out, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  return run_graph(p, q, k, rand_proj, glob, nullptr, nullptr, lsh_out, workspace, workspace_bytes,
+                   stream, 1);
+}
+
+int ssa_merge(const ssa_graph_params* p, const int32_t* lsh, const int32_t* glob,
+              const int32_t* win, int32_t Kw, const int32_t* self_idx, const int32_t* true_max,
+              int32_t* nb_out, uint8_t* valid_out, void* stream) {
+  if (!p) return fail(SSA_ERR_INVALID, "params is NULL");
+  if (p->B < 1 || p->H < 1 || p->N < 1 || p->A < 1 || p->K < 1 || p->G < 0 || Kw < 0)
+    return fail(SSA_ERR_INVALID, "bad merge geometry");
+  if (!lsh || !nb_out || !valid_out || !true_max || (Kw > 0 && !win))
+    return fail(SSA_ERR_INVALID, "NULL lsh/win/true_max/nb_out/valid_out");
+  if (p->G > 0 && !glob) return fail(SSA_ERR_INVALID, "glob is NULL but G > 0");
+  ssa::MergeDev m;
+  memset(&m, 0, sizeof(m));
+  m.B = p->B; m.H = p->H; m.N = p->N; m.A = p->A; m.Kw = Kw; m.G = p->G;
+  const int kall = Kw + p->G + p->A;
+  m.Wout = self_idx ? (p->K - 1 < kall ? p->K - 1 : kall) + 1 : (p->K < kall ? p->K : kall);
+  m.lsh = lsh; m.glob = glob; m.win = win; m.self_idx = self_idx; m.true_max = true_max;
+  m.nb = nb_out; m.valid = valid_out;
+  cudaError_t e = ssa::launch_merge(m, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorInvalidConfiguration)
+    return fail(SSA_ERR_UNSUPPORTED, "window + LSH width (%d) too large for the merge kernel", Kw + p->A);
+  if (e != cudaSuccess) return cuda_fail(e, "merge launch");
+  return SSA_OK;
+}
+
+int ssa_hash_ids(const void* x, int32_t dtype, int32_t B, int32_t heads, int32_t rows, int32_t d,
+                 int64_t sb, int64_t sh, int64_t sn, const float* rand_proj, int32_t R,
+                 int32_t max_p, int32_t p_eff, int32_t* ids_out, void* stream) {
+  int rc;
+  if (dtype != SSA_F32 && dtype != SSA_BF16) return fail(SSA_ERR_INVALID, "bad dtype");
+  if (B < 1 || heads < 1 || rows < 1 || d < 1 || R < 1 || p_eff < 1 || p_eff > max_p || max_p > 12)
+    return fail(SSA_ERR_INVALID, "bad hash geometry");
+  if ((rc = check_rows("x", x, dtype, d, sb, sh, sn))) return rc;
+  if (!rand_proj || !aligned(rand_proj, 16) || !ids_out) return fail(SSA_ERR_INVALID, "bad pointers");
+  cudaError_t e = ssa::launch_hash_ids(x, dtype, B, heads, rows, d, sb, sh, sn, rand_proj, R, max_p,
+                                       p_eff, ids_out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "hash launch");
+  return SSA_OK;
+}
+
+static int check_attn(const ssa_attn_params* p, const void* q, const void* k, const void* v,
+                      const void* nb, const uint8_t* valid) {
+  int rc;
+  if (!p) return fail(SSA_ERR_INVALID, "params is NULL");
+  if (p->B < 1 || p->H < 1 || p->n_kv < 1 || p->N < 1 || p->M < 1 || p->d < 1 || p->Kn < 1)
+    return fail(SSA_ERR_INVALID, "B,H,n_kv,N,M,d,Kn must be >= 1");
+  if (p->H % p->n_kv)
+    return fail(SSA_ERR_INVALID, "num_heads (%d) must be divisible by num_kv_heads (%d)", p->H, p->n_kv);
+  if (p->dtype != SSA_F32 && p->dtype != SSA_BF16) return fail(SSA_ERR_INVALID, "dtype must be F32 or BF16");
+  if (p->d > 256) return fail(SSA_ERR_UNSUPPORTED, "attention supports head dim <= 256 (got %d)", p->d);
+  if (p->Kn > 8192) return fail(SSA_ERR_UNSUPPORTED, "at most 8192 neighbor slots");
+  if ((rc = check_rows("q", q, p->dtype, p->d, p->q_sb, p->q_sh, p->q_sn))) return rc;
+  if ((rc = check_rows("k", k, p->dtype, p->d, p->k_sb, p->k_sh, p->k_sm))) return rc;
+  if ((rc = check_rows("v", v, p->dtype, p->d, p->v_sb, p->v_sh, p->v_sm))) return rc;
+  if (!nb || !valid) return fail(SSA_ERR_INVALID, "neighbors/valid are NULL");
+  return SSA_OK;
+}
+
+static ssa::AttnDev attn_dev(const ssa_attn_params* p) {
+  ssa::AttnDev a;
+  memset(&a, 0, sizeof(a));
+  a.B = p->B; a.H = p->H; a.n_kv = p->n_kv; a.rep = p->H / p->n_kv; a.N = p->N; a.M = p->M;
+  a.d = p->d; a.Kn = p->Kn; a.dtype = p->dtype; a.nb_i64 = p->nb_i64; a.fp32w = p->fp32_weights;
+  a.scale = p->scale;
+  a.q_sb = p->q_sb; a.q_sh = p->q_sh; a.q_sn = p->q_sn;
+  a.k_sb = p->k_sb; a.k_sh = p->k_sh; a.k_sm = p->k_sm;
+  a.v_sb = p->v_sb; a.v_sh = p->v_sh; a.v_sm = p->v_sm;
+  a.o_sb = p->o_sb; a.o_sh = p->o_sh; a.o_sn = p->o_sn;
+  return a;
+}
+
+int ssa_attn_fwd(const ssa_attn_params* p, const void* q, const void* k, const void* v,
+                 const void* nb, const uint8_t* valid, void* out, float* lse, void* stream) {
+  int rc;
+  if ((rc = check_attn(p, q, k, v, nb, valid))) return rc;
+  if ((rc = check_rows("out", out, p->dtype, p->d, p->o_sb, p->o_sh, p->o_sn))) return rc;
+  ssa::AttnDev a = attn_dev(p);
+  a.q = q; a.k = k; a.v = v; a.nb = nb; a.valid = valid; a.out = out; a.lse = lse;
+  cudaError_t e = ssa::launch_attn_fwd(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attention forward launch");
+  return SSA_OK;
+}
+
+size_t ssa_attn_bwd_workspace_size(const ssa_attn_params* p) {
+  if (!p || p->B < 1 || p->H < 1 || p->N < 1 || p->Kn < 1) return 0;
+  ssa::AttnDev a = attn_dev(p);
+  return ssa::attn_bwd_workspace_layout(a, nullptr, nullptr);
+}
+
+int ssa_attn_bwd(const ssa_attn_params* p, const void* q, const void* k, const void* v,
+                 const void* nb, const uint8_t* valid, const void* dO, const float* lse, void* dq,
+                 void* dk, void* dv, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc;
+  if ((rc = check_attn(p, q, k, v, nb, valid))) return rc;
+  if ((rc = check_rows("dO", dO, p->dtype, p->d, p->o_sb, p->o_sh, p->o_sn))) return rc;
+  if ((rc = check_rows("dq", dq, p->dtype, p->d, p->o_sb, p->o_sh, p->o_sn))) return rc;
+  if (!lse || !dk || !dv) return fail(SSA_ERR_INVALID, "lse/dk/dv are NULL");
+  const int64_t E = (int64_t)p->B * p->H * p->N * p->Kn;
+  if (E >= (int64_t(1) << 31)) return fail(SSA_ERR_UNSUPPORTED, "too many edges (%lld)", (long long)E);
+  if ((int64_t)p->B * p->n_kv * p->M >= (int64_t(1) << 31))
+    return fail(SSA_ERR_UNSUPPORTED, "B * n_kv * M too large");
+  ssa::AttnDev a = attn_dev(p);
+  const size_t need = ssa::attn_bwd_workspace_layout(a, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need)
+    return fail(SSA_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  ssa::attn_bwd_workspace_layout(a, &a, workspace);
+  a.q = q; a.k = k; a.v = v; a.nb = nb; a.valid = valid; a.dO = dO; a.lse_in = lse;
+  a.dq = dq; a.dk = dk; a.dv = dv;
+  cudaError_t e = ssa::launch_attn_bwd(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attention backward launch");
+  return SSA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,756 @@
+// ssa_graph.cu -- LSH neighbor-graph build for sm_100a.
+//
+// Replaces LSHGraphBuilder.forward + WindowGraphBuilder + GlobalGraphBuilder +
+// merge_neighbors of the reference (sparse_attention.py:357-1089). The
+// reference materialises, per query, R x (1 + probes) x C candidate slots,
+// deduplicates them with two sorts, gathers every candidate key row and
+// runs a chunked top-k. Here the same result is produced without ever
+// materialising a candidate list:
+//
+//   1. k_hash_keys    per key row: R bucket ids (fp32 sign tests), and for
+//                     every (64-key word, round, bucket) a 64-bit membership
+//                     mask, built with warp match + one atomicOr per bucket.
+//   2. k_bucket_trim  per (kv slice, round, bucket): keeps the first C members
+//                     (ascending key index = the stable bucket order), records
+//                     the bucket size and the C-th member, and marks the
+//                     round's overflow pad key perm[M-1] (the largest key of
+//                     the highest non-empty bucket).
+//   3. k_select_merge per query row (one thread): hashes the query, ORs the
+//                     masks of its R x (1+T) buckets into a 64-bit candidate
+//                     word per 64-key tile, scores exactly those candidates
+//                     from a shared-memory key tile and keeps the top-A in a
+//                     shared-memory min-heap. The few keys whose eligibility
+//                     is not plain membership (pad keys, causal self, empty-
+//                     bucket fallbacks) are resolved by replaying the
+//                     reference's slot order for that one key. Finally the
+//                     LSH set is merged with the window and the globals
+//                     (sorted, deduplicated, self first) straight into the
+//                     neighbor output.
+//
+// Why this equals the reference: a candidate entry survives the reference's
+// cross-round dedup iff it is valid and no earlier slot holds the same key.
+// For an ordinary key x (not a pad key, not causal self, not an empty-bucket
+// fallback of this row) every slot holding x is a valid bucket member, so x
+// is eligible iff it is a member (rank < C) of at least one of the row's
+// buckets -- exactly the OR of the masks. The special keys are replayed.
+#include "ssa_common.cuh"
+#include "ssa_internal.h"
+
+namespace ssa {
+
+// ---------------------------------------------------------------------------
+// 1. Key hashing + bucket membership masks
+// ---------------------------------------------------------------------------
+template <int DT>
+__global__ void __launch_bounds__(256) k_hash_keys(GraphDev g) {
+  extern __shared__ __align__(16) float s_planes[];  // R * p * d
+  const int bg = blockIdx.y;
+  const int b = bg / g.n_kv, gk = bg % g.n_kv;
+  const int pd = g.p * g.d;
+  for (int i = threadIdx.x; i < g.R * pd; i += blockDim.x) {
+    const int r = i / pd, rem = i - r * pd;
+    s_planes[i] = g.rp[(int64_t)r * g.max_p * g.d + rem];
+  }
+  __syncthreads();
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  const bool act = m < g.M;
+  const unsigned amask = __ballot_sync(0xffffffffu, act);
+  if (!act) return;
+  const int lane = threadIdx.x & 31;
+  const int wbase = m - lane;  // multiple of 32
+  const void* row = row_ptr<DT>(g.k, b * g.k_sb + gk * g.k_sh + (int64_t)m * g.k_sm);
+  for (int r = 0; r < g.R; ++r) {
+    uint32_t code = 0;
+    for (int j = 0; j < g.p; ++j) {
+      const float* pl = s_planes + (r * g.p + j) * g.d;
+      float s0 = 0.f, s1 = 0.f;
+      for (int t = 0; t < g.d; t += 4) {
+        const float4 x = load4<DT>(row, t);
+        const float4 w = *reinterpret_cast<const float4*>(pl + t);
+        s0 = fmaf(x.x, w.x, s0);
+        s1 = fmaf(x.y, w.y, s1);
+        s0 = fmaf(x.z, w.z, s0);
+        s1 = fmaf(x.w, w.w, s1);
+      }
+      if (s0 + s1 > 0.f) code |= 1u << j;  // proj > 0, strict (:589)
+    }
+    g.kcode[((int64_t)bg * g.R + r) * g.M + m] = (uint16_t)code;
+    const unsigned peers = __match_any_sync(amask, code);
+    if (lane == __ffs(peers) - 1) {
+      const unsigned long long bits = (unsigned long long)peers << (wbase & 63);
+      atomicOr(&g.bmap[(((int64_t)bg * g.W + (wbase >> 6)) * g.R + r) * g.NB + code], bits);
+    }
+    // perm[M-1] of the stable sort = largest key of the highest bucket.
+    const uint32_t packed = (code << 20) | (uint32_t)m;
+    const uint32_t mx = __reduce_max_sync(amask, packed);
+    if (lane == __ffs(amask) - 1) atomicMax(&g.pmax[bg * g.R + r], mx);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 2. Keep the first C members of every bucket (stable order), sizes, C-th member
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_bucket_trim(GraphDev g) {
+  const int bg = blockIdx.x / g.R, r = blockIdx.x % g.R;
+  for (int u = threadIdx.x; u < g.NB; u += blockDim.x) {
+    int run = 0, last = -1;
+    for (int w = 0; w < g.W; ++w) {
+      unsigned long long* ptr = &g.bmap[(((int64_t)bg * g.W + w) * g.R + r) * g.NB + u];
+      unsigned long long x = *ptr;
+      if (!x) continue;
+      const int c = __popcll(x);
+      if (run >= g.C) {
+        *ptr = 0ull;
+      } else if (run + c > g.C) {
+        int need = g.C - run;
+        unsigned long long keep = 0ull;
+        while (need--) {
+          const unsigned long long lo = x & (~x + 1ull);
+          keep |= lo;
+          x ^= lo;
+        }
+        *ptr = keep;
+        last = w * 64 + 63 - __clzll(keep);
+      } else {
+        last = w * 64 + 63 - __clzll(x);
+      }
+      run += c;
+    }
+    g.bsize[(bg * g.R + r) * g.NB + u] = run;
+    g.lastc[(bg * g.R + r) * g.NB + u] = last;
+  }
+  if (threadIdx.x == 0) {
+    const uint32_t P = g.pmax[bg * g.R + r] & 0xFFFFFu;
+    atomicOr(&g.pmask[(int64_t)bg * g.W + (P >> 6)], 1ull << (P & 63));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 3. Per-row selection (+ merge)
+// ---------------------------------------------------------------------------
+// Shared-memory arrays are interleaved by row: element i of row t lives at
+// [i * rows + t], so 32 threads touching their own element i hit 32 banks.
+template <typename KT>
+struct RowHeap {
+  float* s;
+  KT* k;
+  int rows, t;
+  __device__ float sc(int i) const { return s[i * rows + t]; }
+  __device__ int key(int i) const { return (int)k[i * rows + t]; }
+  __device__ void set(int i, float v, int kk) {
+    s[i * rows + t] = v;
+    k[i * rows + t] = (KT)kk;
+  }
+  // Min-heap on score: place (x, kx) at i and sift down within size.
+  __device__ void sift_score(int i, int size, float x, int kx) {
+    while (true) {
+      const int l = 2 * i + 1;
+      if (l >= size) break;
+      int c = l;
+      float cv = sc(l);
+      if (l + 1 < size) {
+        const float rv = sc(l + 1);
+        if (rv < cv) { c = l + 1; cv = rv; }
+      }
+      if (cv < x) { set(i, cv, key(c)); i = c; } else break;
+    }
+    set(i, x, kx);
+  }
+  __device__ void heapify_score(int size) {
+    for (int i = size / 2 - 1; i >= 0; --i) sift_score(i, size, sc(i), key(i));
+  }
+  // Max-heap on key (for an ascending in-place key sort).
+  __device__ void sift_key(int i, int size, float x, int kx) {
+    while (true) {
+      const int l = 2 * i + 1;
+      if (l >= size) break;
+      int c = l;
+      int cv = key(l);
+      if (l + 1 < size) {
+        const int rv = key(l + 1);
+        if (rv > cv) { c = l + 1; cv = rv; }
+      }
+      if (cv > kx) { set(i, sc(c), cv); i = c; } else break;
+    }
+    set(i, x, kx);
+  }
+  __device__ void sort_keys_ascending(int size) {
+    for (int i = size / 2 - 1; i >= 0; --i) sift_key(i, size, sc(i), key(i));
+    for (int e = size - 1; e > 0; --e) {
+      const float x = sc(e);
+      const int kx = key(e);
+      set(e, sc(0), key(0));
+      sift_key(0, e, x, kx);
+    }
+  }
+  // Descending by score (the reference's topk order): min-heap sort.
+  __device__ void sort_scores_descending(int size, bool is_heap) {
+    if (!is_heap) heapify_score(size);
+    for (int e = size - 1; e > 0; --e) {
+      const float x = sc(e);
+      const int kx = key(e);
+      set(e, sc(0), key(0));
+      sift_score(0, e, x, kx);
+    }
+  }
+};
+
+__device__ __forceinline__ bool key_member(const GraphDev& g, int bg, int r, int u, int x) {
+  if (x < 0 || x >= g.M) return false;
+  if (g.kcode[((int64_t)bg * g.R + r) * g.M + x] != (uint16_t)u) return false;
+  const unsigned long long w =
+      __ldg(&g.bmap[(((int64_t)bg * g.W + (x >> 6)) * g.R + r) * g.NB + u]);
+  return (w >> (x & 63)) & 1ull;
+}
+
+// Replays the reference's slot order (round-major, primary bucket then
+// probes, slot c = 0..C-1) for one key x and reports whether x's FIRST slot
+// is valid -- the cross-round dedup rule of sparse_attention.py:884-890.
+__device__ bool replay_first_valid(const GraphDev& g, const uint16_t* tids, int rows, int t,
+                                   int bg, int n, int x) {
+  for (int tt = 0; tt < g.NT; ++tt) {
+    const int r = tt / (1 + g.Te);
+    const int u = tids[tt * rows + t];
+    const int sz = g.bsize[(bg * g.R + r) * g.NB + u];
+    if (sz == 0) {  // empty bucket: [glob..., 0, ...], all valid (:711-737)
+      const int lim = g.G < g.C ? g.G : g.C;
+      for (int c = 0; c < lim; ++c)
+        if (g.glob[c] == x) return true;
+      if (g.G < g.C && x == 0) return true;
+      continue;
+    }
+    bool real;
+    if (g.causal && x > n) real = false;  // future keys only appear as n
+    else if (g.causal && x == n)          // n itself, or any future member mapped to n
+      real = g.lastc[(bg * g.R + r) * g.NB + u] > n || key_member(g, bg, r, u, n);
+    else
+      real = key_member(g, bg, r, u, x);
+    if (real) return true;
+    if (sz < g.C) {  // overflow slots hold perm[M-1], invalid (:686-696)
+      int P = (int)(g.pmax[bg * g.R + r] & 0xFFFFFu);
+      if (g.causal && P > n) P = n;
+      if (P == x) return false;
+    }
+  }
+  return false;
+}
+
+template <int DT, int D>
+__device__ __forceinline__ float dot_row_global(const float* q, const void* row, int d) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+  for (int i = 0; i < D; i += 4) {
+    if (i < d) {
+      const float4 x = load4<DT>(row, i);
+      s0 = fmaf(q[i], x.x, s0);
+      s1 = fmaf(q[i + 1], x.y, s1);
+      s2 = fmaf(q[i + 2], x.z, s2);
+      s3 = fmaf(q[i + 3], x.w, s3);
+    }
+  }
+  return (s0 + s1) + (s2 + s3);
+}
+
+template <int DT, int D, typename KT>
+__global__ void k_select_merge(GraphDev g, int mode) {
+  // mode: 0 = build_graph (merge into nb/valid, optional lsh set out)
+  //       1 = lsh_select (LSH output only, reference topk order)
+  constexpr int KTILE = 64;
+  constexpr int KS = D + 4;  // padded row stride (floats) of the key tile
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int rows = blockDim.x;
+  float* Ks = reinterpret_cast<float*>(smem);
+  float* hs = Ks + KTILE * KS;
+  KT* hk = reinterpret_cast<KT*>(hs + (size_t)g.A * rows);
+  uint16_t* tids = reinterpret_cast<uint16_t*>(hk + (size_t)g.A * rows);
+  int32_t* gs = reinterpret_cast<int32_t*>(
+      (reinterpret_cast<uintptr_t>(tids + (size_t)g.NT * rows) + 3) & ~uintptr_t(3));
+
+  const int bh = blockIdx.y;
+  const int b = bh / g.H, h = bh % g.H;
+  const int gk = h / g.rep;
+  const int bg = b * g.n_kv + gk;
+  const int t = threadIdx.x;
+  const int n = blockIdx.x * rows + t;
+  const bool act = n < g.N;
+  const int n_hi = min(g.N, (int)(blockIdx.x + 1) * rows) - 1;
+
+  // Sorted unique globals for the merge (:1039-1061 only needs the set).
+  if (mode == 0 && t == 0) {
+    int ng = 0;
+    for (int i = 0; i < g.G; ++i) {
+      const int v = g.glob[i];
+      int j = ng - 1;
+      bool dup = false;
+      for (int z = 0; z < ng; ++z) dup |= gs[z] == v;
+      if (dup) continue;
+      while (j >= 0 && gs[j] > v) { gs[j + 1] = gs[j]; --j; }
+      gs[j + 1] = v;
+      ++ng;
+    }
+    gs[g.G] = ng;  // count stored after the list
+  }
+
+  // ---- query row, hash ids, probe ids --------------------------------------
+  float q[D];
+#pragma unroll
+  for (int i = 0; i < D; ++i) q[i] = 0.f;
+  bool any_empty = false;
+  if (act) {
+    const void* qrow = row_ptr<DT>(g.q, b * g.q_sb + h * g.q_sh + (int64_t)n * g.q_sn);
+#pragma unroll
+    for (int i = 0; i < D; i += 4) {
+      if (i < g.d) {
+        const float4 x = load4<DT>(qrow, i);
+        q[i] = x.x; q[i + 1] = x.y; q[i + 2] = x.z; q[i + 3] = x.w;
+      }
+    }
+    for (int r = 0; r < g.R; ++r) {
+      float proj[12];
+      uint32_t id = 0;
+      for (int j = 0; j < g.p; ++j) {
+        const float* pl = g.rp + ((int64_t)r * g.max_p + j) * g.d;
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < D; i += 4) {
+          if (i < g.d) {
+            const float4 w = __ldg(reinterpret_cast<const float4*>(pl + i));
+            s0 = fmaf(q[i], w.x, s0);
+            s1 = fmaf(q[i + 1], w.y, s1);
+            s0 = fmaf(q[i + 2], w.z, s0);
+            s1 = fmaf(q[i + 3], w.w, s1);
+          }
+        }
+        const float s = s0 + s1;
+        proj[j] = s;
+        if (s > 0.f) id |= 1u << j;
+      }
+      tids[(r * (1 + g.Te)) * rows + t] = (uint16_t)id;
+      // Step-wise multi-probe (:599-646): probe tt flips the bit with the
+      // tt-th smallest |proj| of the ORIGINAL id; ties keep plane order.
+      uint32_t used = 0;
+      for (int tt = 0; tt < g.Te; ++tt) {
+        int best = -1;
+        float bmag = 0.f;
+        for (int j = 0; j < g.p; ++j) {
+          if ((used >> j) & 1u) continue;
+          const float a = fabsf(proj[j]);
+          if (best < 0 || a < bmag) { best = j; bmag = a; }
+        }
+        used |= 1u << best;
+        tids[(r * (1 + g.Te) + 1 + tt) * rows + t] = (uint16_t)(id ^ (1u << best));
+      }
+    }
+    for (int tt = 0; tt < g.NT; ++tt) {
+      const int r = tt / (1 + g.Te);
+      if (g.bsize[(bg * g.R + r) * g.NB + tids[tt * rows + t]] == 0) any_empty = true;
+    }
+  }
+
+  // ---- dense candidate scan -------------------------------------------------
+  RowHeap<KT> heap{hs, hk, rows, t};
+  int cnt = 0;
+  auto push = [&](float s, int key) {
+    if (cnt < g.A) {
+      heap.set(cnt, s, key);
+      if (++cnt == g.A) heap.heapify_score(g.A);
+    } else if (s > heap.sc(0)) {
+      heap.sift_score(0, g.A, s, key);
+    }
+  };
+  const int nkt = g.causal ? min(g.W, (n_hi >> 6) + 1) : g.W;
+  const char* kbase = reinterpret_cast<const char*>(row_ptr<DT>(g.k, b * g.k_sb + gk * g.k_sh));
+  for (int kt = 0; kt < nkt; ++kt) {
+    const int key0 = kt * KTILE;
+    __syncthreads();
+    for (int e = t * 4; e < KTILE * D; e += rows * 4) {
+      const int j = e / D, i = e - j * D;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (key0 + j < g.M && i < g.d)
+        x = load4<DT>(row_ptr<DT>(kbase, (int64_t)(key0 + j) * g.k_sm), i);
+      *reinterpret_cast<float4*>(Ks + j * KS + i) = x;
+    }
+    __syncthreads();
+    if (!act) continue;
+    const unsigned long long* bm = g.bmap + ((int64_t)bg * g.W + kt) * g.R * g.NB;
+    unsigned long long w = 0ull;
+    for (int tt = 0; tt < g.NT; ++tt) {
+      const int r = tt / (1 + g.Te);
+      w |= __ldg(bm + r * g.NB + tids[tt * rows + t]);
+    }
+    w &= ~__ldg(g.pmask + (int64_t)bg * g.W + kt);
+    if (g.causal) {  // keys < n only; n itself is a special key
+      const int lim = n - key0;
+      if (lim <= 0) w = 0ull;
+      else if (lim < 64) w &= (1ull << lim) - 1ull;
+    }
+    while (w) {
+      const int j = __ffsll((long long)w) - 1;
+      w &= w - 1ull;
+      const float* kr = Ks + j * KS;
+      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+      for (int i = 0; i < D; i += 4) {
+        const float4 x = *reinterpret_cast<const float4*>(kr + i);
+        s0 = fmaf(q[i], x.x, s0);
+        s1 = fmaf(q[i + 1], x.y, s1);
+        s2 = fmaf(q[i + 2], x.z, s2);
+        s3 = fmaf(q[i + 3], x.w, s3);
+      }
+      push((s0 + s1) + (s2 + s3), key0 + j);
+    }
+  }
+  if (!act) return;
+
+  // ---- special keys: replay the reference slot order -----------------------
+  // Candidate list: the R pad keys, causal self, and (only if one of this
+  // row's buckets is empty) the empty-bucket fallback entries.
+  const int lim_g = g.G < g.C ? g.G : g.C;
+  const int nspec = g.R + 1 + (any_empty ? lim_g + 1 : 0);
+  auto spec_at = [&](int i) -> int {
+    if (i < g.R) return (int)(g.pmax[bg * g.R + i] & 0xFFFFFu);
+    if (i == g.R) return g.causal ? n : -1;
+    i -= g.R + 1;
+    if (i < lim_g) return g.glob[i];
+    return g.G < g.C ? 0 : -1;
+  };
+  for (int i = 0; i < nspec; ++i) {
+    const int x = spec_at(i);
+    if (x < 0 || x >= g.M) continue;  // not a key of this sequence (e.g. self when N > M)
+    if (i < g.R && g.causal && x > n) continue;  // a future pad key never appears as itself
+    bool dup = false;
+    for (int z = 0; z < i && !dup; ++z) dup = spec_at(z) == x;
+    if (dup) continue;
+    if (!replay_first_valid(g, tids, rows, t, bg, n, x)) continue;
+    // Keys the dense scan may have already taken: not a pad key, not causal self.
+    const bool scanned = !((__ldg(g.pmask + (int64_t)bg * g.W + (x >> 6)) >> (x & 63)) & 1ull) &&
+                         !(g.causal && x >= n);
+    if (scanned) {
+      bool present = false;
+      for (int z = 0; z < cnt && !present; ++z) present = heap.key(z) == x;
+      if (present) continue;
+    }
+    const void* krow = row_ptr<DT>(kbase, (int64_t)x * g.k_sm);
+    push(dot_row_global<DT, D>(q, krow, g.d), x);
+  }
+
+  // ---- outputs -----------------------------------------------------------------
+  // Slots the reference fills from -inf scores get glob[j] (j < G) else 0
+  // (:948-957); only the set matters to the merge, where the globals are
+  // present anyway, so the merge adds just key 0 when such a slot exists.
+  const bool add_zero = max(cnt, g.G) < g.A;
+  if (mode == 1) {
+    heap.sort_scores_descending(cnt, cnt == g.A);
+    int32_t* out = g.lsh + ((int64_t)bh * g.N + n) * g.A;
+    for (int j = 0; j < g.A; ++j)
+      out[j] = j < cnt ? heap.key(j) : (j < g.G ? g.glob[j] : 0);
+    return;
+  }
+  if (g.lsh) {
+    int32_t* out = g.lsh + ((int64_t)bh * g.N + n) * g.A;
+    for (int j = 0; j < g.A; ++j)
+      out[j] = j < cnt ? heap.key(j) : (j < g.G ? g.glob[j] : 0);
+  }
+  heap.sort_keys_ascending(cnt);
+  // Three-way merge of ascending streams: LSH keys, the window, the globals
+  // (+ key 0 from the fallback). Self is excluded and takes slot 0 (:1043-1076).
+  int32_t* nbo = g.nb + ((int64_t)bh * g.N + n) * g.Wout;
+  uint8_t* vo = g.valid + ((int64_t)bh * g.N + n) * g.Wout;
+  int slot = 0;
+  if (!g.is_cross) {
+    nbo[0] = min(n, g.M - 1);  // merge's final clamp to the true maximum index
+    vo[0] = 1;
+    slot = 1;
+  }
+  const int ng = gs[g.G];
+  const int kw = g.is_cross ? 0 : 2 * g.window + 1;
+  int il = 0, iw = 0, ig = 0;
+  bool zero_pending = add_zero;
+  int last = -1;
+  const int BIG = 0x7fffffff;
+  while (slot < g.Wout) {
+    int vl = il < cnt ? heap.key(il) : BIG;
+    int vw = BIG;
+    if (iw < kw) {
+      const int o = iw - g.window;
+      int idx = (g.causal && o > 0) ? n : n + o;
+      idx = idx < 0 ? 0 : (idx > g.M - 1 ? g.M - 1 : idx);
+      vw = idx;
+    }
+    const int vg = ig < ng ? gs[ig] : BIG;
+    const int vz = zero_pending ? 0 : BIG;
+    int v = min(min(vl, vw), min(vg, vz));
+    if (v == BIG) break;
+    if (v == vl) ++il;
+    else if (v == vw) ++iw;
+    else if (v == vg) ++ig;
+    else zero_pending = false;
+    if (v == last || (!g.is_cross && v == n)) continue;
+    last = v;
+    nbo[slot] = v;
+    vo[slot] = 1;
+    ++slot;
+  }
+  for (; slot < g.Wout; ++slot) {
+    nbo[slot] = 0;
+    vo[slot] = 0;
+  }
+}
+
+// Standalone merge_neighbors (sparse_attention.py:966-1089) over explicit
+// inputs: per row, the window row and the LSH row are sorted together
+// (in-place heap sort, ascending) and merged with the sorted unique globals;
+// entries equal to the row's self index are dropped, duplicates collapse,
+// self (if any) takes slot 0 and everything is clamped to [0, true_max].
+__device__ void int_sift(int32_t* a, int rows, int t, int i, int size, int x) {
+  while (true) {
+    const int l = 2 * i + 1;
+    if (l >= size) break;
+    int c = l;
+    int cv = a[l * rows + t];
+    if (l + 1 < size) {
+      const int rv = a[(l + 1) * rows + t];
+      if (rv > cv) { c = l + 1; cv = rv; }
+    }
+    if (cv > x) { a[i * rows + t] = cv; i = c; } else break;
+  }
+  a[i * rows + t] = x;
+}
+
+__global__ void k_merge_rows(MergeDev m) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int rows = blockDim.x;
+  int32_t* buf = reinterpret_cast<int32_t*>(smem);
+  int32_t* gs = buf + (size_t)(m.Kw + m.A) * rows;
+  const int t = threadIdx.x;
+  if (t == 0) {
+    int ng = 0;
+    for (int i = 0; i < m.G; ++i) {
+      const int v = m.glob[i];
+      bool dup = false;
+      for (int z = 0; z < ng; ++z) dup |= gs[z] == v;
+      if (dup) continue;
+      int j = ng - 1;
+      while (j >= 0 && gs[j] > v) { gs[j + 1] = gs[j]; --j; }
+      gs[j + 1] = v;
+      ++ng;
+    }
+    gs[m.G] = ng;
+  }
+  __syncthreads();
+  const int64_t row = (int64_t)blockIdx.x * rows + t;
+  if (row >= (int64_t)m.B * m.H * m.N) return;
+  const int n = (int)(row % m.N);
+  const int tm = *m.true_max;
+  const int L = m.Kw + m.A;
+  for (int j = 0; j < m.Kw; ++j) buf[j * rows + t] = m.win[(int64_t)n * m.Kw + j];
+  for (int j = 0; j < m.A; ++j) buf[(m.Kw + j) * rows + t] = m.lsh[row * m.A + j];
+  for (int i = L / 2 - 1; i >= 0; --i) int_sift(buf, rows, t, i, L, buf[i * rows + t]);
+  for (int e = L - 1; e > 0; --e) {
+    const int x = buf[e * rows + t];
+    buf[e * rows + t] = buf[t];
+    int_sift(buf, rows, t, 0, e, x);
+  }
+  int32_t* nbo = m.nb + row * m.Wout;
+  uint8_t* vo = m.valid + row * m.Wout;
+  int slot = 0;
+  const bool has_self = m.self_idx != nullptr;
+  const int self = has_self ? m.self_idx[row] : 0;
+  if (has_self) {
+    nbo[0] = self < 0 ? 0 : (self > tm ? tm : self);
+    vo[0] = 1;
+    slot = 1;
+  }
+  const int ng = gs[m.G];
+  int il = 0, ig = 0;
+  bool first = true;
+  int last = 0;
+  const int BIG = 0x7fffffff;
+  while (slot < m.Wout) {
+    const int vl = il < L ? buf[il * rows + t] : BIG;
+    const int vg = ig < ng ? gs[ig] : BIG;
+    const int v = min(vl, vg);
+    if (il >= L && ig >= ng) break;
+    if (v == vl && il < L) ++il; else ++ig;
+    if ((!first && v == last) || (has_self && v == self)) continue;
+    first = false;
+    last = v;
+    nbo[slot] = v < 0 ? 0 : (v > tm ? tm : v);
+    vo[slot] = v <= tm;
+    ++slot;
+  }
+  for (; slot < m.Wout; ++slot) {
+    nbo[slot] = 0;
+    vo[slot] = 0;
+  }
+}
+
+// Query/key hash ids only (the reference's _hash), for the ssa_hash_ids API.
+template <int DT>
+__global__ void __launch_bounds__(256) k_hash_ids(const void* x, int B, int heads, int rows_n,
+                                                  int d, int64_t sb, int64_t sh, int64_t sn,
+                                                  const float* rp, int R, int max_p, int p,
+                                                  int32_t* out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = (int64_t)B * heads * rows_n;
+  if (i >= total) return;
+  const int n = (int)(i % rows_n);
+  const int64_t bh = i / rows_n;
+  const int b = (int)(bh / heads), h = (int)(bh % heads);
+  const void* row = row_ptr<DT>(x, b * sb + h * sh + (int64_t)n * sn);
+  for (int r = 0; r < R; ++r) {
+    uint32_t code = 0;
+    for (int j = 0; j < p; ++j) {
+      const float* pl = rp + ((int64_t)r * max_p + j) * d;
+      float s0 = 0.f, s1 = 0.f;
+      for (int t = 0; t < d; t += 4) {
+        const float4 v = load4<DT>(row, t);
+        const float4 w = __ldg(reinterpret_cast<const float4*>(pl + t));
+        s0 = fmaf(v.x, w.x, s0);
+        s1 = fmaf(v.y, w.y, s1);
+        s0 = fmaf(v.z, w.z, s0);
+        s1 = fmaf(v.w, w.w, s1);
+      }
+      if (s0 + s1 > 0.f) code |= 1u << j;
+    }
+    out[(bh * R + r) * rows_n + n] = (int32_t)code;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host launchers
+// ---------------------------------------------------------------------------
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+size_t graph_workspace_layout(const GraphShape& s, GraphDev* g) {
+  const int64_t BG = (int64_t)s.B * s.n_kv;
+  const int64_t W = (s.M + 63) / 64;
+  const int64_t NB = int64_t(1) << s.p;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  const size_t o_kcode = take(sizeof(uint16_t) * BG * s.R * s.M);
+  const size_t o_zero_begin = off;
+  const size_t o_bmap = take(sizeof(unsigned long long) * BG * W * s.R * NB);
+  const size_t o_pmask = take(sizeof(unsigned long long) * BG * W);
+  const size_t o_pmax = take(sizeof(uint32_t) * BG * s.R);
+  const size_t o_zero_end = off;
+  const size_t o_bsize = take(sizeof(int32_t) * BG * s.R * NB);
+  const size_t o_lastc = take(sizeof(int32_t) * BG * s.R * NB);
+  const size_t o_lsh = s.need_lsh_scratch ? take(sizeof(int32_t) * (size_t)s.B * s.H * s.N * s.A) : 0;
+  if (g) {
+    char* base = static_cast<char*>(g->ws);
+    g->kcode = reinterpret_cast<uint16_t*>(base + o_kcode);
+    g->bmap = reinterpret_cast<unsigned long long*>(base + o_bmap);
+    g->pmask = reinterpret_cast<unsigned long long*>(base + o_pmask);
+    g->pmax = reinterpret_cast<uint32_t*>(base + o_pmax);
+    g->bsize = reinterpret_cast<int32_t*>(base + o_bsize);
+    g->lastc = reinterpret_cast<int32_t*>(base + o_lastc);
+    if (s.need_lsh_scratch) g->lsh = reinterpret_cast<int32_t*>(base + o_lsh);
+    g->zero_off = o_zero_begin;
+    g->zero_bytes = o_zero_end - o_zero_begin;
+  }
+  return off;
+}
+
+static size_t select_smem(int D, int rows, int A, int NT, int G, int key_bytes) {
+  return (size_t)64 * (D + 4) * 4 + (size_t)A * rows * (4 + key_bytes) +
+         (size_t)NT * rows * 2 + 4 + (size_t)(G + 1) * 4 + 16;
+}
+
+int choose_select_rows(const GraphDev& g, int* rows_out, size_t* smem_out) {
+  const int D = g.d <= 32 ? 32 : (g.d <= 64 ? 64 : 128);
+  const int kb = g.M <= 65536 ? 2 : 4;
+  const size_t budget2 = 113 * 1024, budget1 = 227 * 1024;
+  for (int rows : {128, 64, 32}) {
+    const size_t sm = select_smem(D, rows, g.A, g.NT, g.G, kb);
+    if (sm <= budget2) { *rows_out = rows; *smem_out = sm; return 0; }
+  }
+  for (int rows : {64, 32}) {
+    const size_t sm = select_smem(D, rows, g.A, g.NT, g.G, kb);
+    if (sm <= budget1) { *rows_out = rows; *smem_out = sm; return 0; }
+  }
+  return 1;
+}
+
+template <typename F>
+static cudaError_t set_smem(F* fn, size_t bytes) {
+  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+template <int DT, int D, typename KT>
+static cudaError_t launch_select_t(const GraphDev& g, int mode, int rows, size_t smem,
+                                   cudaStream_t st) {
+  auto fn = k_select_merge<DT, D, KT>;
+  cudaError_t e = set_smem(fn, smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((g.N + rows - 1) / rows, g.B * g.H);
+  fn<<<grid, rows, smem, st>>>(g, mode);
+  return cudaGetLastError();
+}
+
+template <int DT>
+static cudaError_t launch_select_dt(const GraphDev& g, int mode, int rows, size_t smem,
+                                    cudaStream_t st) {
+  const bool k16 = g.M <= 65536;
+  if (g.d <= 32) return k16 ? launch_select_t<DT, 32, uint16_t>(g, mode, rows, smem, st)
+                            : launch_select_t<DT, 32, uint32_t>(g, mode, rows, smem, st);
+  if (g.d <= 64) return k16 ? launch_select_t<DT, 64, uint16_t>(g, mode, rows, smem, st)
+                            : launch_select_t<DT, 64, uint32_t>(g, mode, rows, smem, st);
+  return k16 ? launch_select_t<DT, 128, uint16_t>(g, mode, rows, smem, st)
+             : launch_select_t<DT, 128, uint32_t>(g, mode, rows, smem, st);
+}
+
+cudaError_t launch_graph(const GraphDev& g, int mode, cudaStream_t st) {
+  cudaError_t e;
+  e = cudaMemsetAsync(static_cast<char*>(g.ws) + g.zero_off, 0, g.zero_bytes, st);
+  if (e != cudaSuccess) return e;
+  {
+    const size_t sm = (size_t)g.R * g.p * g.d * sizeof(float);
+    dim3 grid((g.M + 255) / 256, g.B * g.n_kv);
+    if (g.dtype == kDtF32) {
+      if ((e = set_smem(k_hash_keys<kDtF32>, sm)) != cudaSuccess) return e;
+      k_hash_keys<kDtF32><<<grid, 256, sm, st>>>(g);
+    } else {
+      if ((e = set_smem(k_hash_keys<kDtBF16>, sm)) != cudaSuccess) return e;
+      k_hash_keys<kDtBF16><<<grid, 256, sm, st>>>(g);
+    }
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  k_bucket_trim<<<g.B * g.n_kv * g.R, 256, 0, st>>>(g);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  int rows;
+  size_t smem;
+  if (choose_select_rows(g, &rows, &smem)) return cudaErrorInvalidConfiguration;
+  return g.dtype == kDtF32 ? launch_select_dt<kDtF32>(g, mode, rows, smem, st)
+                           : launch_select_dt<kDtBF16>(g, mode, rows, smem, st);
+}
+
+cudaError_t launch_merge(const MergeDev& m, cudaStream_t st) {
+  int rows = 128;
+  auto bytes = [&](int r) { return (size_t)(m.Kw + m.A) * r * 4 + (size_t)(m.G + 1) * 4; };
+  while (bytes(rows) > 200 * 1024 && rows > 32) rows /= 2;
+  if (bytes(rows) > 227 * 1024) return cudaErrorInvalidConfiguration;
+  cudaError_t e = set_smem(k_merge_rows, bytes(rows));
+  if (e != cudaSuccess) return e;
+  const int64_t total = (int64_t)m.B * m.H * m.N;
+  k_merge_rows<<<(unsigned)((total + rows - 1) / rows), rows, bytes(rows), st>>>(m);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_hash_ids(const void* x, int dtype, int B, int heads, int rows, int d,
+                            int64_t sb, int64_t sh, int64_t sn, const float* rp, int R,
+                            int max_p, int p, int32_t* out, cudaStream_t st) {
+  const int64_t total = (int64_t)B * heads * rows;
+  const unsigned grid = (unsigned)((total + 255) / 256);
+  if (dtype == kDtF32)
+    k_hash_ids<kDtF32><<<grid, 256, 0, st>>>(x, B, heads, rows, d, sb, sh, sn, rp, R, max_p, p, out);
+  else
+    k_hash_ids<kDtBF16><<<grid, 256, 0, st>>>(x, B, heads, rows, d, sb, sh, sn, rp, R, max_p, p, out);
+  return cudaGetLastError();
+}
+
+}  // namespace ssa

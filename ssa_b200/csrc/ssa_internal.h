@@ -1,0 +1,90 @@
+// ssa_internal.h -- device-side parameter blocks and launchers shared by the
+// kernel files and the C ABI (ssa_capi.cu). Not part of the public ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace ssa {
+
+struct GraphShape {
+  int B, H, n_kv, N, M, d, R, p, A;
+  bool need_lsh_scratch;
+};
+
+// Everything a graph-build kernel needs, passed by value.
+struct GraphDev {
+  int B, H, n_kv, rep, N, M, d, dtype;
+  int R, max_p, p, C, Te, NT, NB, W, A;
+  int causal, is_cross, window, G, Wout;
+  int64_t q_sb, q_sh, q_sn, k_sb, k_sh, k_sm;
+  const void* q;
+  const void* k;
+  const float* rp;        // (R, max_p, d)
+  const int32_t* glob;    // (G,)
+  // workspace
+  void* ws;
+  size_t zero_off, zero_bytes;
+  uint16_t* kcode;                // [BG][R][M] bucket id of every key
+  unsigned long long* bmap;       // [BG][W][R][NB] first-C member masks
+  unsigned long long* pmask;      // [BG][W] pad keys perm_r[M-1]
+  uint32_t* pmax;                 // [BG][R] (bucket << 20 | key) of perm_r[M-1]
+  int32_t* bsize;                 // [BG][R][NB]
+  int32_t* lastc;                 // [BG][R][NB] key at rank min(size, C) - 1
+  // outputs
+  int32_t* lsh;                   // [B][H][N][A]
+  int32_t* nb;                    // [B][H][N][Wout]
+  uint8_t* valid;                 // [B][H][N][Wout]
+};
+
+size_t graph_workspace_layout(const GraphShape& s, GraphDev* g);
+int choose_select_rows(const GraphDev& g, int* rows_out, size_t* smem_out);
+cudaError_t launch_graph(const GraphDev& g, int mode, cudaStream_t st);
+struct MergeDev {
+  int B, H, N, A, Kw, G, Wout;
+  const int32_t* lsh;       // [B][H][N][A]
+  const int32_t* glob;      // [G]
+  const int32_t* win;       // [N][Kw]
+  const int32_t* self_idx;  // [B][H][N] or null (cross-attention)
+  const int32_t* true_max;  // device scalar
+  int32_t* nb;              // [B][H][N][Wout]
+  uint8_t* valid;
+};
+cudaError_t launch_merge(const MergeDev& m, cudaStream_t st);
+cudaError_t launch_hash_ids(const void* x, int dtype, int B, int heads, int rows, int d,
+                            int64_t sb, int64_t sh, int64_t sn, const float* rp, int R,
+                            int max_p, int p, int32_t* out, cudaStream_t st);
+
+struct AttnDev {
+  int B, H, n_kv, rep, N, M, d, Kn, dtype, nb_i64, fp32w;
+  float scale;
+  int64_t q_sb, q_sh, q_sn, k_sb, k_sh, k_sm, v_sb, v_sh, v_sm, o_sb, o_sh, o_sn;
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* nb;
+  const uint8_t* valid;
+  void* out;
+  float* lse;
+  // backward
+  const void* dO;
+  const float* lse_in;
+  void* dq;
+  void* dk;
+  void* dv;
+  float* ep;          // [rows][Kn] value weight per edge
+  float* eds;         // [rows][Kn] scale * dS per edge
+  uint32_t* ekey;     // [rows][Kn] bg * M + key, or the sentinel BG * M
+  uint32_t* eid;      // [rows][Kn] edge id (row * Kn + slot)
+  uint32_t* skey;     // sorted keys
+  uint32_t* sid;      // edge ids in sorted order
+  void* sort_tmp;
+  size_t sort_tmp_bytes;
+};
+
+cudaError_t launch_attn_fwd(const AttnDev& a, cudaStream_t st);
+size_t attn_bwd_workspace_layout(const AttnDev& a, AttnDev* out, void* ws);
+cudaError_t launch_attn_bwd(const AttnDev& a, cudaStream_t st);
+
+}  // namespace ssa

@@ -1,0 +1,292 @@
+"""Torch-facing wrappers of the C ABI: tensors in, tensors out.
+
+Every function here launches sm_100a kernels from libssa_b200.so on the
+current CUDA stream. Tensors must live on a CUDA device; there is no CPU
+path. Query-side tensors are (B, H, N, d) and key/value tensors
+(B, n_kv, M, d), each with any strides whose last axis is contiguous -- so
+the (B, N, H*d) outputs of the q/k/v projections are consumed without a
+transpose or a GQA repeat.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import AttnParams, GraphParams, SSA_BF16, SSA_F32, check
+
+
+def _require_cuda(*ts: torch.Tensor):
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("ssa_b200 runs on CUDA tensors only (there is no CPU path); "
+                               f"got a tensor on {t.device}")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} vs {t.device}")
+    return dev
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return SSA_F32
+    if t.dtype == torch.bfloat16:
+        return SSA_BF16
+    raise NotImplementedError(f"ssa_b200 kernels take float32 or bfloat16 tensors, got {t.dtype}")
+
+
+def _rows(t: torch.Tensor) -> Tuple[torch.Tensor, int, int, int]:
+    """A 4-D tensor with a contiguous last axis and 4-element-aligned strides
+    (copying only if needed), plus its first three strides."""
+    if t.dim() != 4:
+        raise ValueError(f"expected a 4-D tensor, got shape {tuple(t.shape)}")
+    s = t.stride()
+    es = t.element_size()
+    ok = (s[3] == 1 and all(x % 4 == 0 for x in s[:3]) and
+          t.data_ptr() % (16 if es == 4 else 8) == 0)
+    if not ok:
+        t = t.contiguous()
+        s = t.stride()
+    return t, s[0], s[1], s[2]
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream(dev: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def graph_params(q, k, *, R, max_p, p_eff, C, T, A, causal, is_cross, K, window, G):
+    B, H, N, d = q.shape
+    Bk, n_kv, M, dk = k.shape
+    if Bk != B or dk != d:
+        raise ValueError(f"q {tuple(q.shape)} and k {tuple(k.shape)} disagree")
+    if H % n_kv:
+        raise ValueError(f"num_heads ({H}) must be divisible by num_kv_heads ({n_kv})")
+    p = GraphParams()
+    p.B, p.H, p.n_kv, p.N, p.M, p.d = B, H, n_kv, N, M, d
+    p.dtype = _dtype_code(q)
+    p.R, p.max_p, p.p_eff, p.C, p.T, p.A = R, max_p, p_eff, C, T, A
+    p.causal, p.is_cross, p.K, p.window, p.G = int(causal), int(is_cross), K, window, G
+    return p
+
+
+def _graph_inputs(q, k, rand_proj, glob):
+    _require_cuda(q, k, rand_proj, glob)
+    if q.dtype != k.dtype:
+        raise ValueError(f"q and k dtypes differ ({q.dtype} vs {k.dtype})")
+    q, qsb, qsh, qsn = _rows(q)
+    k, ksb, ksh, ksm = _rows(k)
+    rp = rand_proj.detach().to(torch.float32).contiguous()
+    g = glob.to(torch.int32).contiguous() if glob is not None else None
+    return q, (qsb, qsh, qsn), k, (ksb, ksh, ksm), rp, g
+
+
+def build_graph(q: torch.Tensor, k: torch.Tensor, rand_proj: torch.Tensor, glob: torch.Tensor, *,
+                R: int, max_p: int, p_eff: int, C: int, T: int, A: int, causal: bool,
+                is_cross: bool, K: int, window: int, want_lsh: bool = False):
+    """SparseAttention.build_graph on the GPU. Returns int32 neighbors
+    (B,H,N,W), uint8 valid (B,H,N,W) and, if asked, the int32 LSH set."""
+    q, qs, k, ks, rp, g = _graph_inputs(q, k, rand_proj, glob)
+    G = g.numel() if g is not None else 0
+    p = graph_params(q, k, R=R, max_p=max_p, p_eff=p_eff, C=C, T=T, A=A, causal=causal,
+                     is_cross=is_cross, K=K, window=window, G=G)
+    p.q_sb, p.q_sh, p.q_sn = qs
+    p.k_sb, p.k_sh, p.k_sm = ks
+    L = _lib.load()
+    W = L.ssa_graph_width(ctypes.byref(p))
+    ws_bytes = L.ssa_graph_workspace_size(ctypes.byref(p))
+    if ws_bytes == 0:
+        check(L.ssa_build_graph(ctypes.byref(p), None, None, None, None, None, None, None, None, 0,
+                                None), "ssa_build_graph")
+    B, H, N = q.shape[:3]
+    dev = q.device
+    nb = torch.empty((B, H, N, W), dtype=torch.int32, device=dev)
+    valid = torch.empty((B, H, N, W), dtype=torch.uint8, device=dev)
+    lsh = torch.empty((B, H, N, A), dtype=torch.int32, device=dev) if want_lsh else None
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    check(L.ssa_build_graph(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(rp), _ptr(g), _ptr(nb),
+                            _ptr(valid), _ptr(lsh), _ptr(ws), ws_bytes, _stream(dev)),
+          "ssa_build_graph")
+    return (nb, valid, lsh) if want_lsh else (nb, valid)
+
+
+def lsh_select(q, k, rand_proj, glob, *, R, max_p, p_eff, C, T, A, causal):
+    """LSHGraphBuilder.forward on the GPU: (B,H,N,A) int32, reference order."""
+    q, qs, k, ks, rp, g = _graph_inputs(q, k, rand_proj, glob)
+    G = g.numel() if g is not None else 0
+    p = graph_params(q, k, R=R, max_p=max_p, p_eff=p_eff, C=C, T=T, A=A, causal=causal,
+                     is_cross=False, K=1, window=0, G=G)
+    p.q_sb, p.q_sh, p.q_sn = qs
+    p.k_sb, p.k_sh, p.k_sm = ks
+    L = _lib.load()
+    ws_bytes = L.ssa_graph_workspace_size(ctypes.byref(p))
+    if ws_bytes == 0:
+        check(L.ssa_lsh_select(ctypes.byref(p), None, None, None, None, None, None, 0, None),
+              "ssa_lsh_select")
+    B, H, N = q.shape[:3]
+    dev = q.device
+    out = torch.empty((B, H, N, A), dtype=torch.int32, device=dev)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    check(L.ssa_lsh_select(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(rp), _ptr(g), _ptr(out),
+                           _ptr(ws), ws_bytes, _stream(dev)), "ssa_lsh_select")
+    return out
+
+
+def merge(win: torch.Tensor, glob: torch.Tensor, lsh: torch.Tensor, self_idx: Optional[torch.Tensor],
+          total_k: int):
+    """merge_neighbors on the GPU for explicit window/global/LSH/self
+    tensors. Returns int32 neighbors and uint8 valid."""
+    _require_cuda(win, glob, lsh, self_idx)
+    B, H, N, A = lsh.shape
+    win32 = win.to(torch.int32).reshape(N, -1).contiguous()
+    Kw = win32.shape[1]
+    g = glob.to(torch.int32).reshape(-1).contiguous()
+    l32 = lsh.to(torch.int32).contiguous()
+    is_cross = self_idx is None
+    s32 = None
+    if not is_cross:
+        s32 = self_idx.to(torch.int32).expand(B, H, N).contiguous()
+    # true_max_idx: one maximum over the whole combined tensor (:1031), kept
+    # on the device (no host sync).
+    parts = [l32.max()]
+    if Kw:
+        parts.append(win32.max())
+    if g.numel():
+        parts.append(g.max())
+    true_max = torch.stack(parts).max().reshape(1).contiguous()
+    p = GraphParams()
+    p.B, p.H, p.N, p.A, p.K, p.G = B, H, N, A, total_k, g.numel()
+    p.causal, p.is_cross = 0, int(is_cross)
+    kall = Kw + g.numel() + A
+    W = min(total_k, kall) if is_cross else min(total_k - 1, kall) + 1
+    dev = lsh.device
+    nb = torch.empty((B, H, N, W), dtype=torch.int32, device=dev)
+    valid = torch.empty((B, H, N, W), dtype=torch.uint8, device=dev)
+    check(_lib.load().ssa_merge(ctypes.byref(p), _ptr(l32), _ptr(g), _ptr(win32) if Kw else None,
+                                Kw, _ptr(s32), _ptr(true_max), _ptr(nb), _ptr(valid), _stream(dev)),
+          "ssa_merge")
+    return nb, valid
+
+
+def hash_ids(x: torch.Tensor, rand_proj: torch.Tensor, R: int, max_p: int, p_eff: int):
+    """Per-round bucket ids of x (B, heads, rows, d): (B*heads, R, rows) int32."""
+    _require_cuda(x, rand_proj)
+    x, sb, sh, sn = _rows(x)
+    B, Hh, Nr, d = x.shape
+    rp = rand_proj.detach().to(torch.float32).contiguous()
+    out = torch.empty((B * Hh, R, Nr), dtype=torch.int32, device=x.device)
+    check(_lib.load().ssa_hash_ids(_ptr(x), _dtype_code(x), B, Hh, Nr, d, sb, sh, sn, _ptr(rp), R,
+                                   max_p, p_eff, _ptr(out), _stream(x.device)), "ssa_hash_ids")
+    return out
+
+
+def _attn_params(q, k, v, nb, scale, fp32w, o_strides):
+    B, H, N, d = q.shape
+    _, n_kv, M, _ = k.shape
+    if v.shape != k.shape:
+        raise ValueError(f"k {tuple(k.shape)} and v {tuple(v.shape)} differ")
+    if nb.shape[:3] != (B, H, N):
+        raise ValueError(f"neighbors {tuple(nb.shape)} do not match q {tuple(q.shape)}")
+    p = AttnParams()
+    p.B, p.H, p.n_kv, p.N, p.M, p.d, p.Kn = B, H, n_kv, N, M, d, nb.shape[3]
+    p.dtype = _dtype_code(q)
+    p.nb_i64 = int(nb.dtype == torch.int64)
+    p.fp32_weights = int(bool(fp32w))
+    p.scale = float(scale)
+    p.o_sb, p.o_sh, p.o_sn = o_strides
+    return p
+
+
+def _index_inputs(nb, valid):
+    if nb.dtype not in (torch.int32, torch.int64):
+        nb = nb.to(torch.int32)
+    nb = nb.contiguous()
+    if valid.dtype == torch.bool:
+        valid = valid.contiguous().view(torch.uint8)
+    else:
+        valid = valid.to(torch.uint8).contiguous()
+    return nb, valid
+
+
+def attn_fwd(q, k, v, nb, valid, scale: float, fp32w: bool, out: Optional[torch.Tensor] = None,
+             want_lse: bool = True):
+    """Gather attention forward. `out` (B,H,N,d) may be a strided view (for
+    example of a (B,N,H,d) buffer); returns (out, lse)."""
+    _require_cuda(q, k, v, nb, valid)
+    if not (q.dtype == k.dtype == v.dtype):
+        raise ValueError("q, k, v must share one dtype")
+    q, *qs = _rows(q)
+    k, *ks = _rows(k)
+    v, *vs = _rows(v)
+    nb, valid = _index_inputs(nb, valid)
+    B, H, N, d = q.shape
+    if out is None:
+        out = torch.empty((B, N, H, d), dtype=q.dtype, device=q.device).permute(0, 2, 1, 3)
+    o = out.stride()
+    p = _attn_params(q, k, v, nb, scale, fp32w, (o[0], o[1], o[2]))
+    p.q_sb, p.q_sh, p.q_sn = qs
+    p.k_sb, p.k_sh, p.k_sm = ks
+    p.v_sb, p.v_sh, p.v_sm = vs
+    lse = torch.empty((B, H, N), dtype=torch.float32, device=q.device) if want_lse else None
+    check(_lib.load().ssa_attn_fwd(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(nb), _ptr(valid),
+                                   _ptr(out), _ptr(lse), _stream(q.device)), "ssa_attn_fwd")
+    return out, lse
+
+
+def attn_bwd(q, k, v, nb, valid, dO, lse, scale: float, fp32w: bool):
+    """Gradients of sum(out * dO): dq (B,H,N,d), dk/dv (B,n_kv,M,d)."""
+    _require_cuda(q, k, v, nb, valid, dO, lse)
+    q, *qs = _rows(q)
+    k, *ks = _rows(k)
+    v, *vs = _rows(v)
+    dO = dO.to(q.dtype)
+    dO, *os_ = _rows(dO)
+    nb, valid = _index_inputs(nb, valid)
+    dq = torch.empty_strided(dO.shape, dO.stride(), dtype=q.dtype, device=q.device)
+    dk = torch.empty(k.shape, dtype=q.dtype, device=q.device)
+    dv = torch.empty(v.shape, dtype=q.dtype, device=q.device)
+    p = _attn_params(q, k, v, nb, scale, fp32w, tuple(os_))
+    p.q_sb, p.q_sh, p.q_sn = qs
+    p.k_sb, p.k_sh, p.k_sm = ks
+    p.v_sb, p.v_sh, p.v_sm = vs
+    L = _lib.load()
+    ws_bytes = L.ssa_attn_bwd_workspace_size(ctypes.byref(p))
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
+    check(L.ssa_attn_bwd(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(nb), _ptr(valid), _ptr(dO),
+                         _ptr(lse.contiguous()), _ptr(dq), _ptr(dk), _ptr(dv), _ptr(ws), ws_bytes,
+                         _stream(q.device)), "ssa_attn_bwd")
+    return dq, dk, dv
+
+
+class GatherAttention(torch.autograd.Function):
+    """Autograd wrapper: the graph (nb, valid) is non-differentiable, as in
+    the reference (routing decisions are sign tests and top-k)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, nb, valid, scale, fp32w):
+        out, lse = attn_fwd(q, k, v, nb, valid, scale, fp32w)
+        ctx.save_for_backward(q, k, v, nb, valid, lse)
+        ctx.scale, ctx.fp32w = scale, fp32w
+        ctx.mark_non_differentiable()
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, nb, valid, lse = ctx.saved_tensors
+        dq, dk, dv = attn_bwd(q, k, v, nb, valid, dout, lse, ctx.scale, ctx.fp32w)
+        return dq, dk, dv, None, None, None, None
+
+
+def gather_attention(q, k, v, nb, valid, scale: float, fp32w: bool = False):
+    if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
+        return GatherAttention.apply(q, k, v, nb, valid, scale, fp32w)
+    return attn_fwd(q, k, v, nb, valid, scale, fp32w, want_lse=False)[0]

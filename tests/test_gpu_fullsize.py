@@ -1,0 +1,105 @@
+"""Parity at the BASELINE configurations' full sizes.
+
+The GPU builds the graph for the whole configuration; the oracle recomputes
+one (batch, kv-group) slice -- all query rows for the causal / cross
+configs, a block of query rows for the long non-causal one (its LSH result
+does not depend on the row index, so the block is selected alone and then
+merged at its true positions) -- and the rows are compared exactly, with
+rescore ties attributed. Over the whole GPU graph, size-independent
+properties are checked: self in slot 0, strictly ascending unique real
+neighbors, padding only at the end, no future index under causal masking
+other than a global token (the reference does not filter globals), every
+index inside [0, M).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from parity import compare_graphs
+
+from ssa_b200 import ops
+from ssa_b200.workloads import WORKLOADS, make_module, make_x, project
+
+pytestmark = pytest.mark.gpu
+
+
+def _check_structure(nb, valid, N, M, causal, cross, glob):
+    nb = nb.long()
+    v = valid.bool()
+    assert bool(((nb >= 0) & (nb < M)).all())
+    start = 0 if cross else 1
+    if not cross:
+        ar = torch.arange(N, device=nb.device).view(1, 1, N)
+        assert bool((nb[..., 0] == torch.clamp(ar, max=M - 1)).all())
+        assert bool(v[..., 0].all())
+    body, vb = nb[..., start:], v[..., start:]
+    assert bool((vb[..., 1:] <= vb[..., :-1]).all()), "valid slots must form a prefix"
+    assert bool(((body[..., 1:] > body[..., :-1]) | ~vb[..., 1:]).all()), "not strictly ascending"
+    if causal and not cross:
+        n = torch.arange(N, device=nb.device).view(1, 1, N, 1)
+        is_glob = torch.zeros_like(v)
+        for gidx in glob:
+            is_glob |= nb == gidx
+        assert not bool(((nb > n) & v & ~is_glob).any()), "future index leaked"
+
+
+@pytest.mark.parametrize("cfg,rows", [("c2", None), ("c3", (8192, 12288)), ("c5", None)])
+def test_fullsize_graph_slice_matches_oracle(cfg, rows, cuda):
+    w = WORKLOADS[cfg]
+    m = make_module(w, cuda)
+    x, kv = make_x(w, cuda)
+    q, k, v = project(m, x, kv)
+    lsh = m.lsh_builder
+    glob = m._glob(w.M, cuda).cpu().tolist()
+    nb, valid = m._graph(q, k, w.M, w.causal and not w.cross, w.cross)
+    torch.cuda.synchronize()
+    _check_structure(nb, valid, w.N, w.M, w.causal, w.cross, glob)
+    heads = slice(0, min(w.H // w.n_kv, 4))
+    qs = q[0:1, heads].float()
+    if rows is not None:
+        qs = qs[:, :, rows[0]:rows[1]]
+    qs_np = qs.contiguous().cpu().numpy()
+    ks_np = k[0:1, 0:1].float().contiguous().cpu().numpy()
+    rp = lsh.rand_proj.cpu().numpy()
+    if rows is None:
+        ora_nb, ora_valid = O.build_graph(qs_np, ks_np, rp, n_kv=1, K=w.K, w=w.window, G=w.G,
+                                          glob_idx=list(w.glob) if w.glob else None, R=w.R,
+                                          maxP=w.max_p, T=w.T, causal=w.causal, is_cross=w.cross)
+        g_nb, g_va = nb[0:1, heads], valid[0:1, heads]
+    else:
+        assert not w.causal
+        lsh_o = O.lsh_select(qs_np, ks_np, rp, n_kv=1, R=w.R, maxP=w.max_p,
+                             p=lsh.compute_effective_p(w.M, lsh.C, lsh.max_P), C=lsh.C, T=w.T,
+                             A=lsh.output_width(w.M, m.lsh_k), causal=False, glob=glob)
+        pad = np.zeros(lsh_o.shape[:2] + (rows[0],) + lsh_o.shape[3:], dtype=np.int32)
+        ora_nb, ora_valid = O.merge(np.concatenate([pad, lsh_o], axis=2), M=w.M, w=w.window,
+                                    glob=glob, causal=False, is_cross=w.cross, K=w.K)
+        ora_nb, ora_valid = ora_nb[:, :, rows[0]:], ora_valid[:, :, rows[0]:]
+        g_nb = nb[0:1, heads, rows[0]:rows[1]]
+        g_va = valid[0:1, heads, rows[0]:rows[1]]
+    res = compare_graphs(g_nb.cpu().numpy(), g_va.cpu().numpy().astype(bool), ora_nb, ora_valid,
+                         qs_np, ks_np, 1)
+    print(cfg, {kk: res[kk] for kk in ("rows", "mismatched", "ties")})
+    assert res["unexplained"] == 0, res
+    assert res["ties"] <= max(2, res["rows"] // 1000), res
+
+
+@pytest.mark.parametrize("cfg", ["c2", "c5"])
+def test_fullsize_attention_slice_matches_oracle(cfg, cuda):
+    w = WORKLOADS[cfg]
+    m = make_module(w, cuda)
+    x, kv = make_x(w, cuda)
+    q, k, v = project(m, x, kv)
+    nb, valid = m._graph(q, k, w.M, w.causal and not w.cross, w.cross)
+    out = ops.gather_attention(q, k, v, nb, valid, m.scale)
+    torch.cuda.synchronize()
+    assert bool(torch.isfinite(out.float()).all())
+    hs = slice(0, min(w.H // w.n_kv, 2))
+    o_ref, _ = O.attn_fwd(q[0:1, hs].float().contiguous().cpu().numpy(),
+                          k[0:1, 0:1].float().contiguous().cpu().numpy(),
+                          v[0:1, 0:1].float().contiguous().cpu().numpy(),
+                          nb[0:1, hs].cpu().numpy(), valid[0:1, hs].cpu().numpy().astype(bool),
+                          scale=m.scale, lowp=True, fp32_w=False)
+    mine = out[0:1, hs].float().cpu().numpy()
+    assert np.abs(mine - o_ref).max() <= 2e-2 * np.abs(o_ref).max()
