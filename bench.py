@@ -48,6 +48,8 @@ def parse_args(argv=None):
     ap.add_argument("--impl", default="ssa", choices=["ssa", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the workload's batch size (profiling a smaller case)")
     ap.add_argument("--baseline-slices", type=int, default=2,
                     help="(batch, kv-group) slices in the CPU baseline sample")
     return ap.parse_args(argv)
@@ -170,6 +172,8 @@ def run_gpu(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=dev)
     w = WORKLOADS[args.workload]
+    if args.batch:
+        w = type(w)(**{**w.__dict__, "B": args.batch})
     m = make_module(w, dev)
     x, kv = make_x(w, dev, seed=1 + rank)
     q, k, v = project(m, x, kv)

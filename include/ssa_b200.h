@@ -164,6 +164,10 @@ SSA_API int ssa_attn_bwd(const ssa_attn_params* p, const void* q, const void* k,
                  void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
                  void* stream);
 
+/* Error code recorded by a kernel whose bounded wait on an on-chip barrier
+ * ran out (0 = none); synchronises with the device. clear != 0 resets it. */
+SSA_API int32_t ssa_device_error(int32_t clear);
+
 /* Human-readable text for the last error on this host thread. */
 SSA_API const char* ssa_last_error(void);
 

@@ -55,6 +55,7 @@ SIGNATURES = {
     "ssa_attn_bwd_workspace_size": (_sz, [ctypes.POINTER(AttnParams)]),
     "ssa_attn_bwd": (ctypes.c_int, [ctypes.POINTER(AttnParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                     _vp, _vp, _vp, _vp, _sz, _vp]),
+    "ssa_device_error": (_i32, [_i32]),
     "ssa_last_error": (ctypes.c_char_p, []),
     "ssa_abi_version": (_i32, []),
 }

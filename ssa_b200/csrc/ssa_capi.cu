@@ -91,6 +91,7 @@ ssa::GraphDev dev_of(const ssa_graph_params* p) {
   g.NT = g.R * (1 + g.Te);
   g.NB = 1 << g.p;
   g.W = (p->M + 63) / 64;
+  g.Wpad = (g.W + 1) / 2 * 2;
   g.A = p->A; g.causal = p->causal; g.is_cross = p->is_cross; g.window = p->window; g.G = p->G;
   g.Wout = graph_width(p);
   g.q_sb = p->q_sb; g.q_sh = p->q_sh; g.q_sn = p->q_sn;
@@ -126,6 +127,8 @@ const char* ssa_last_error(void) { return g_err; }
 
 int32_t ssa_abi_version(void) { return 100; }
 
+int32_t ssa_device_error(int32_t clear) { return ssa::read_device_error(clear); }
+
 int32_t ssa_graph_width(const ssa_graph_params* p) { return p ? graph_width(p) : -1; }
 
 size_t ssa_graph_workspace_size(const ssa_graph_params* p) {
@@ -149,7 +152,7 @@ static int run_graph(const ssa_graph_params* p, const void* q, const void* k, co
   ssa::graph_workspace_layout(shape_of(p, false), &g);
   g.q = q; g.k = k; g.rp = rp; g.glob = glob;
   g.lsh = lsh_out; g.nb = nb_out; g.valid = valid_out;
-  if ((rc = check_select_fits(g))) return rc;
+  if (!ssa::select_tc_supported(g) && (rc = check_select_fits(g))) return rc;
   cudaError_t e = ssa::launch_graph(g, mode, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "graph build launch");
   return SSA_OK;

@@ -35,6 +35,7 @@
 // buckets -- exactly the OR of the masks. The special keys are replayed.
 #include "ssa_common.cuh"
 #include "ssa_internal.h"
+#include "ssa_select_common.cuh"
 
 namespace ssa {
 
@@ -78,7 +79,7 @@ __global__ void __launch_bounds__(256) k_hash_keys(GraphDev g) {
     const unsigned peers = __match_any_sync(amask, code);
     if (lane == __ffs(peers) - 1) {
       const unsigned long long bits = (unsigned long long)peers << (wbase & 63);
-      atomicOr(&g.bmap[(((int64_t)bg * g.W + (wbase >> 6)) * g.R + r) * g.NB + code], bits);
+      atomicOr(&g.bmap[(((int64_t)bg * g.Wpad + (wbase >> 6)) * g.R + r) * g.NB + code], bits);
     }
     // perm[M-1] of the stable sort = largest key of the highest bucket.
     const uint32_t packed = (code << 20) | (uint32_t)m;
@@ -95,7 +96,7 @@ __global__ void __launch_bounds__(256) k_bucket_trim(GraphDev g) {
   for (int u = threadIdx.x; u < g.NB; u += blockDim.x) {
     int run = 0, last = -1;
     for (int w = 0; w < g.W; ++w) {
-      unsigned long long* ptr = &g.bmap[(((int64_t)bg * g.W + w) * g.R + r) * g.NB + u];
+      unsigned long long* ptr = &g.bmap[(((int64_t)bg * g.Wpad + w) * g.R + r) * g.NB + u];
       unsigned long long x = *ptr;
       if (!x) continue;
       const int c = __popcll(x);
@@ -121,136 +122,13 @@ __global__ void __launch_bounds__(256) k_bucket_trim(GraphDev g) {
   }
   if (threadIdx.x == 0) {
     const uint32_t P = g.pmax[bg * g.R + r] & 0xFFFFFu;
-    atomicOr(&g.pmask[(int64_t)bg * g.W + (P >> 6)], 1ull << (P & 63));
+    atomicOr(&g.pmask[(int64_t)bg * g.Wpad + (P >> 6)], 1ull << (P & 63));
   }
 }
 
 // ---------------------------------------------------------------------------
 // 3. Per-row selection (+ merge)
 // ---------------------------------------------------------------------------
-// Shared-memory arrays are interleaved by row: element i of row t lives at
-// [i * rows + t], so 32 threads touching their own element i hit 32 banks.
-template <typename KT>
-struct RowHeap {
-  float* s;
-  KT* k;
-  int rows, t;
-  __device__ float sc(int i) const { return s[i * rows + t]; }
-  __device__ int key(int i) const { return (int)k[i * rows + t]; }
-  __device__ void set(int i, float v, int kk) {
-    s[i * rows + t] = v;
-    k[i * rows + t] = (KT)kk;
-  }
-  // Min-heap on score: place (x, kx) at i and sift down within size.
-  __device__ void sift_score(int i, int size, float x, int kx) {
-    while (true) {
-      const int l = 2 * i + 1;
-      if (l >= size) break;
-      int c = l;
-      float cv = sc(l);
-      if (l + 1 < size) {
-        const float rv = sc(l + 1);
-        if (rv < cv) { c = l + 1; cv = rv; }
-      }
-      if (cv < x) { set(i, cv, key(c)); i = c; } else break;
-    }
-    set(i, x, kx);
-  }
-  __device__ void heapify_score(int size) {
-    for (int i = size / 2 - 1; i >= 0; --i) sift_score(i, size, sc(i), key(i));
-  }
-  // Max-heap on key (for an ascending in-place key sort).
-  __device__ void sift_key(int i, int size, float x, int kx) {
-    while (true) {
-      const int l = 2 * i + 1;
-      if (l >= size) break;
-      int c = l;
-      int cv = key(l);
-      if (l + 1 < size) {
-        const int rv = key(l + 1);
-        if (rv > cv) { c = l + 1; cv = rv; }
-      }
-      if (cv > kx) { set(i, sc(c), cv); i = c; } else break;
-    }
-    set(i, x, kx);
-  }
-  __device__ void sort_keys_ascending(int size) {
-    for (int i = size / 2 - 1; i >= 0; --i) sift_key(i, size, sc(i), key(i));
-    for (int e = size - 1; e > 0; --e) {
-      const float x = sc(e);
-      const int kx = key(e);
-      set(e, sc(0), key(0));
-      sift_key(0, e, x, kx);
-    }
-  }
-  // Descending by score (the reference's topk order): min-heap sort.
-  __device__ void sort_scores_descending(int size, bool is_heap) {
-    if (!is_heap) heapify_score(size);
-    for (int e = size - 1; e > 0; --e) {
-      const float x = sc(e);
-      const int kx = key(e);
-      set(e, sc(0), key(0));
-      sift_score(0, e, x, kx);
-    }
-  }
-};
-
-__device__ __forceinline__ bool key_member(const GraphDev& g, int bg, int r, int u, int x) {
-  if (x < 0 || x >= g.M) return false;
-  if (g.kcode[((int64_t)bg * g.R + r) * g.M + x] != (uint16_t)u) return false;
-  const unsigned long long w =
-      __ldg(&g.bmap[(((int64_t)bg * g.W + (x >> 6)) * g.R + r) * g.NB + u]);
-  return (w >> (x & 63)) & 1ull;
-}
-
-// Replays the reference's slot order (round-major, primary bucket then
-// probes, slot c = 0..C-1) for one key x and reports whether x's FIRST slot
-// is valid -- the cross-round dedup rule of sparse_attention.py:884-890.
-__device__ bool replay_first_valid(const GraphDev& g, const uint16_t* tids, int rows, int t,
-                                   int bg, int n, int x) {
-  for (int tt = 0; tt < g.NT; ++tt) {
-    const int r = tt / (1 + g.Te);
-    const int u = tids[tt * rows + t];
-    const int sz = g.bsize[(bg * g.R + r) * g.NB + u];
-    if (sz == 0) {  // empty bucket: [glob..., 0, ...], all valid (:711-737)
-      const int lim = g.G < g.C ? g.G : g.C;
-      for (int c = 0; c < lim; ++c)
-        if (g.glob[c] == x) return true;
-      if (g.G < g.C && x == 0) return true;
-      continue;
-    }
-    bool real;
-    if (g.causal && x > n) real = false;  // future keys only appear as n
-    else if (g.causal && x == n)          // n itself, or any future member mapped to n
-      real = g.lastc[(bg * g.R + r) * g.NB + u] > n || key_member(g, bg, r, u, n);
-    else
-      real = key_member(g, bg, r, u, x);
-    if (real) return true;
-    if (sz < g.C) {  // overflow slots hold perm[M-1], invalid (:686-696)
-      int P = (int)(g.pmax[bg * g.R + r] & 0xFFFFFu);
-      if (g.causal && P > n) P = n;
-      if (P == x) return false;
-    }
-  }
-  return false;
-}
-
-template <int DT, int D>
-__device__ __forceinline__ float dot_row_global(const float* q, const void* row, int d) {
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-  for (int i = 0; i < D; i += 4) {
-    if (i < d) {
-      const float4 x = load4<DT>(row, i);
-      s0 = fmaf(q[i], x.x, s0);
-      s1 = fmaf(q[i + 1], x.y, s1);
-      s2 = fmaf(q[i + 2], x.z, s2);
-      s3 = fmaf(q[i + 3], x.w, s3);
-    }
-  }
-  return (s0 + s1) + (s2 + s3);
-}
-
 template <int DT, int D, typename KT>
 __global__ void k_select_merge(GraphDev g, int mode) {
   // mode: 0 = build_graph (merge into nb/valid, optional lsh set out)
@@ -275,23 +153,22 @@ __global__ void k_select_merge(GraphDev g, int mode) {
   const bool act = n < g.N;
   const int n_hi = min(g.N, (int)(blockIdx.x + 1) * rows) - 1;
 
-  // Sorted unique globals for the merge (:1039-1061 only needs the set).
-  if (mode == 0 && t == 0) {
+  // Sorted unique globals for the merge (only the set matters to it).
+  if (t == 0) {
     int ng = 0;
     for (int i = 0; i < g.G; ++i) {
       const int v = g.glob[i];
-      int j = ng - 1;
       bool dup = false;
       for (int z = 0; z < ng; ++z) dup |= gs[z] == v;
       if (dup) continue;
+      int j = ng - 1;
       while (j >= 0 && gs[j] > v) { gs[j + 1] = gs[j]; --j; }
       gs[j + 1] = v;
       ++ng;
     }
-    gs[g.G] = ng;  // count stored after the list
+    gs[g.G] = ng;
   }
 
-  // ---- query row, hash ids, probe ids --------------------------------------
   float q[D];
 #pragma unroll
   for (int i = 0; i < D; ++i) q[i] = 0.f;
@@ -305,59 +182,13 @@ __global__ void k_select_merge(GraphDev g, int mode) {
         q[i] = x.x; q[i + 1] = x.y; q[i + 2] = x.z; q[i + 3] = x.w;
       }
     }
-    for (int r = 0; r < g.R; ++r) {
-      float proj[12];
-      uint32_t id = 0;
-      for (int j = 0; j < g.p; ++j) {
-        const float* pl = g.rp + ((int64_t)r * g.max_p + j) * g.d;
-        float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-        for (int i = 0; i < D; i += 4) {
-          if (i < g.d) {
-            const float4 w = __ldg(reinterpret_cast<const float4*>(pl + i));
-            s0 = fmaf(q[i], w.x, s0);
-            s1 = fmaf(q[i + 1], w.y, s1);
-            s0 = fmaf(q[i + 2], w.z, s0);
-            s1 = fmaf(q[i + 3], w.w, s1);
-          }
-        }
-        const float s = s0 + s1;
-        proj[j] = s;
-        if (s > 0.f) id |= 1u << j;
-      }
-      tids[(r * (1 + g.Te)) * rows + t] = (uint16_t)id;
-      // Step-wise multi-probe (:599-646): probe tt flips the bit with the
-      // tt-th smallest |proj| of the ORIGINAL id; ties keep plane order.
-      uint32_t used = 0;
-      for (int tt = 0; tt < g.Te; ++tt) {
-        int best = -1;
-        float bmag = 0.f;
-        for (int j = 0; j < g.p; ++j) {
-          if ((used >> j) & 1u) continue;
-          const float a = fabsf(proj[j]);
-          if (best < 0 || a < bmag) { best = j; bmag = a; }
-        }
-        used |= 1u << best;
-        tids[(r * (1 + g.Te) + 1 + tt) * rows + t] = (uint16_t)(id ^ (1u << best));
-      }
-    }
-    for (int tt = 0; tt < g.NT; ++tt) {
-      const int r = tt / (1 + g.Te);
-      if (g.bsize[(bg * g.R + r) * g.NB + tids[tt * rows + t]] == 0) any_empty = true;
-    }
+    any_empty = hash_row_ids<D>(g, q, bg, tids, rows, t);
   }
 
-  // ---- dense candidate scan -------------------------------------------------
+  // Dense candidate scan over 64-key tiles staged in shared memory; only the
+  // row's candidates (OR of its bucket masks) are scored.
   RowHeap<KT> heap{hs, hk, rows, t};
   int cnt = 0;
-  auto push = [&](float s, int key) {
-    if (cnt < g.A) {
-      heap.set(cnt, s, key);
-      if (++cnt == g.A) heap.heapify_score(g.A);
-    } else if (s > heap.sc(0)) {
-      heap.sift_score(0, g.A, s, key);
-    }
-  };
   const int nkt = g.causal ? min(g.W, (n_hi >> 6) + 1) : g.W;
   const char* kbase = reinterpret_cast<const char*>(row_ptr<DT>(g.k, b * g.k_sb + gk * g.k_sh));
   for (int kt = 0; kt < nkt; ++kt) {
@@ -372,13 +203,13 @@ __global__ void k_select_merge(GraphDev g, int mode) {
     }
     __syncthreads();
     if (!act) continue;
-    const unsigned long long* bm = g.bmap + ((int64_t)bg * g.W + kt) * g.R * g.NB;
+    const unsigned long long* bm = g.bmap + ((int64_t)bg * g.Wpad + kt) * g.R * g.NB;
     unsigned long long w = 0ull;
     for (int tt = 0; tt < g.NT; ++tt) {
       const int r = tt / (1 + g.Te);
       w |= __ldg(bm + r * g.NB + tids[tt * rows + t]);
     }
-    w &= ~__ldg(g.pmask + (int64_t)bg * g.W + kt);
+    w &= ~__ldg(g.pmask + (int64_t)bg * g.Wpad + kt);
     if (g.causal) {  // keys < n only; n itself is a special key
       const int lim = n - key0;
       if (lim <= 0) w = 0ull;
@@ -397,104 +228,11 @@ __global__ void k_select_merge(GraphDev g, int mode) {
         s2 = fmaf(q[i + 2], x.z, s2);
         s3 = fmaf(q[i + 3], x.w, s3);
       }
-      push((s0 + s1) + (s2 + s3), key0 + j);
+      heap.push(cnt, g.A, (s0 + s1) + (s2 + s3), key0 + j);
     }
   }
   if (!act) return;
-
-  // ---- special keys: replay the reference slot order -----------------------
-  // Candidate list: the R pad keys, causal self, and (only if one of this
-  // row's buckets is empty) the empty-bucket fallback entries.
-  const int lim_g = g.G < g.C ? g.G : g.C;
-  const int nspec = g.R + 1 + (any_empty ? lim_g + 1 : 0);
-  auto spec_at = [&](int i) -> int {
-    if (i < g.R) return (int)(g.pmax[bg * g.R + i] & 0xFFFFFu);
-    if (i == g.R) return g.causal ? n : -1;
-    i -= g.R + 1;
-    if (i < lim_g) return g.glob[i];
-    return g.G < g.C ? 0 : -1;
-  };
-  for (int i = 0; i < nspec; ++i) {
-    const int x = spec_at(i);
-    if (x < 0 || x >= g.M) continue;  // not a key of this sequence (e.g. self when N > M)
-    if (i < g.R && g.causal && x > n) continue;  // a future pad key never appears as itself
-    bool dup = false;
-    for (int z = 0; z < i && !dup; ++z) dup = spec_at(z) == x;
-    if (dup) continue;
-    if (!replay_first_valid(g, tids, rows, t, bg, n, x)) continue;
-    // Keys the dense scan may have already taken: not a pad key, not causal self.
-    const bool scanned = !((__ldg(g.pmask + (int64_t)bg * g.W + (x >> 6)) >> (x & 63)) & 1ull) &&
-                         !(g.causal && x >= n);
-    if (scanned) {
-      bool present = false;
-      for (int z = 0; z < cnt && !present; ++z) present = heap.key(z) == x;
-      if (present) continue;
-    }
-    const void* krow = row_ptr<DT>(kbase, (int64_t)x * g.k_sm);
-    push(dot_row_global<DT, D>(q, krow, g.d), x);
-  }
-
-  // ---- outputs -----------------------------------------------------------------
-  // Slots the reference fills from -inf scores get glob[j] (j < G) else 0
-  // (:948-957); only the set matters to the merge, where the globals are
-  // present anyway, so the merge adds just key 0 when such a slot exists.
-  const bool add_zero = max(cnt, g.G) < g.A;
-  if (mode == 1) {
-    heap.sort_scores_descending(cnt, cnt == g.A);
-    int32_t* out = g.lsh + ((int64_t)bh * g.N + n) * g.A;
-    for (int j = 0; j < g.A; ++j)
-      out[j] = j < cnt ? heap.key(j) : (j < g.G ? g.glob[j] : 0);
-    return;
-  }
-  if (g.lsh) {
-    int32_t* out = g.lsh + ((int64_t)bh * g.N + n) * g.A;
-    for (int j = 0; j < g.A; ++j)
-      out[j] = j < cnt ? heap.key(j) : (j < g.G ? g.glob[j] : 0);
-  }
-  heap.sort_keys_ascending(cnt);
-  // Three-way merge of ascending streams: LSH keys, the window, the globals
-  // (+ key 0 from the fallback). Self is excluded and takes slot 0 (:1043-1076).
-  int32_t* nbo = g.nb + ((int64_t)bh * g.N + n) * g.Wout;
-  uint8_t* vo = g.valid + ((int64_t)bh * g.N + n) * g.Wout;
-  int slot = 0;
-  if (!g.is_cross) {
-    nbo[0] = min(n, g.M - 1);  // merge's final clamp to the true maximum index
-    vo[0] = 1;
-    slot = 1;
-  }
-  const int ng = gs[g.G];
-  const int kw = g.is_cross ? 0 : 2 * g.window + 1;
-  int il = 0, iw = 0, ig = 0;
-  bool zero_pending = add_zero;
-  int last = -1;
-  const int BIG = 0x7fffffff;
-  while (slot < g.Wout) {
-    int vl = il < cnt ? heap.key(il) : BIG;
-    int vw = BIG;
-    if (iw < kw) {
-      const int o = iw - g.window;
-      int idx = (g.causal && o > 0) ? n : n + o;
-      idx = idx < 0 ? 0 : (idx > g.M - 1 ? g.M - 1 : idx);
-      vw = idx;
-    }
-    const int vg = ig < ng ? gs[ig] : BIG;
-    const int vz = zero_pending ? 0 : BIG;
-    int v = min(min(vl, vw), min(vg, vz));
-    if (v == BIG) break;
-    if (v == vl) ++il;
-    else if (v == vw) ++iw;
-    else if (v == vg) ++ig;
-    else zero_pending = false;
-    if (v == last || (!g.is_cross && v == n)) continue;
-    last = v;
-    nbo[slot] = v;
-    vo[slot] = 1;
-    ++slot;
-  }
-  for (; slot < g.Wout; ++slot) {
-    nbo[slot] = 0;
-    vo[slot] = 0;
-  }
+  finish_row<DT, D, KT>(g, mode, heap, cnt, tids, rows, t, gs, bh, b, h, gk, bg, n, any_empty);
 }
 
 // Standalone merge_neighbors (sparse_attention.py:966-1089) over explicit
@@ -624,7 +362,7 @@ static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 size_t graph_workspace_layout(const GraphShape& s, GraphDev* g) {
   const int64_t BG = (int64_t)s.B * s.n_kv;
-  const int64_t W = (s.M + 63) / 64;
+  const int64_t W = ((s.M + 63) / 64 + 1) / 2 * 2;  // padded to an even word count
   const int64_t NB = int64_t(1) << s.p;
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -722,6 +460,7 @@ cudaError_t launch_graph(const GraphDev& g, int mode, cudaStream_t st) {
   }
   k_bucket_trim<<<g.B * g.n_kv * g.R, 256, 0, st>>>(g);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if (select_tc_supported(g)) return launch_select_tc(g, mode, st);
   int rows;
   size_t smem;
   if (choose_select_rows(g, &rows, &smem)) return cudaErrorInvalidConfiguration;

@@ -16,7 +16,7 @@ struct GraphShape {
 // Everything a graph-build kernel needs, passed by value.
 struct GraphDev {
   int B, H, n_kv, rep, N, M, d, dtype;
-  int R, max_p, p, C, Te, NT, NB, W, A;
+  int R, max_p, p, C, Te, NT, NB, W, Wpad, A;
   int causal, is_cross, window, G, Wout;
   int64_t q_sb, q_sh, q_sn, k_sb, k_sh, k_sm;
   const void* q;
@@ -41,6 +41,9 @@ struct GraphDev {
 size_t graph_workspace_layout(const GraphShape& s, GraphDev* g);
 int choose_select_rows(const GraphDev& g, int* rows_out, size_t* smem_out);
 cudaError_t launch_graph(const GraphDev& g, int mode, cudaStream_t st);
+bool select_tc_supported(const GraphDev& g);
+cudaError_t launch_select_tc(const GraphDev& g, int mode, cudaStream_t st);
+int read_device_error(int clear);
 struct MergeDev {
   int B, H, N, A, Kw, G, Wout;
   const int32_t* lsh;       // [B][H][N][A]
