@@ -20,7 +20,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 OBJ_DIR = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libssa_b200.so")
-SOURCES = ["ssa_graph.cu", "ssa_select_tc.cu", "ssa_attn.cu", "ssa_capi.cu"]
+SOURCES = ["ssa_graph.cu", "ssa_select_tc.cu", "ssa_select_rows.cu", "ssa_attn.cu", "ssa_capi.cu"]
 HEADERS = ["ssa_common.cuh", "ssa_internal.h", "ssa_select_common.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",

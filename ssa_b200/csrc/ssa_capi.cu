@@ -74,14 +74,6 @@ int check_graph(const ssa_graph_params* p) {
   return SSA_OK;
 }
 
-ssa::GraphShape shape_of(const ssa_graph_params* p, bool need_lsh_scratch) {
-  ssa::GraphShape s;
-  s.B = p->B; s.H = p->H; s.n_kv = p->n_kv; s.N = p->N; s.M = p->M; s.d = p->d;
-  s.R = p->R; s.p = p->p_eff; s.A = p->A;
-  s.need_lsh_scratch = need_lsh_scratch;
-  return s;
-}
-
 ssa::GraphDev dev_of(const ssa_graph_params* p) {
   ssa::GraphDev g;
   memset(&g, 0, sizeof(g));
@@ -133,7 +125,8 @@ int32_t ssa_graph_width(const ssa_graph_params* p) { return p ? graph_width(p) :
 
 size_t ssa_graph_workspace_size(const ssa_graph_params* p) {
   if (check_graph(p)) return 0;
-  return ssa::graph_workspace_layout(shape_of(p, false), nullptr);
+  ssa::GraphDev g = dev_of(p);
+  return ssa::graph_workspace_layout(&g);
 }
 
 static int run_graph(const ssa_graph_params* p, const void* q, const void* k, const float* rp,
@@ -144,15 +137,15 @@ static int run_graph(const ssa_graph_params* p, const void* q, const void* k, co
   if ((rc = check_graph_inputs(p, q, k, rp, glob))) return rc;
   if (mode == 0 && (!nb_out || !valid_out)) return fail(SSA_ERR_INVALID, "nb_out/valid_out are NULL");
   if (mode == 1 && !lsh_out) return fail(SSA_ERR_INVALID, "lsh_out is NULL");
-  const size_t need = ssa::graph_workspace_layout(shape_of(p, false), nullptr);
+  ssa::GraphDev g = dev_of(p);
+  const size_t need = ssa::graph_workspace_layout(&g);
   if (!ws || ws_bytes < need)
     return fail(SSA_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, ws_bytes);
-  ssa::GraphDev g = dev_of(p);
   g.ws = ws;
-  ssa::graph_workspace_layout(shape_of(p, false), &g);
+  ssa::graph_workspace_layout(&g);
   g.q = q; g.k = k; g.rp = rp; g.glob = glob;
   g.lsh = lsh_out; g.nb = nb_out; g.valid = valid_out;
-  if (!ssa::select_tc_supported(g) && (rc = check_select_fits(g))) return rc;
+  if ((rc = check_select_fits(g))) return rc;  // the FMA scan is also the exact fallback
   cudaError_t e = ssa::launch_graph(g, mode, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "graph build launch");
   return SSA_OK;

@@ -145,6 +145,8 @@ __global__ void k_select_merge(GraphDev g, int mode) {
       (reinterpret_cast<uintptr_t>(tids + (size_t)g.NT * rows) + 3) & ~uintptr_t(3));
 
   const int bh = blockIdx.y;
+  // As the exact fallback of the tensor-core path, only flagged 128-row tiles run.
+  if (g.fallback_only && !g.tile_flags[(int64_t)bh * ((g.N + 127) / 128) + (blockIdx.x * rows) / 128]) return;
   const int b = bh / g.H, h = bh % g.H;
   const int gk = h / g.rep;
   const int bg = b * g.n_kv + gk;
@@ -360,34 +362,56 @@ __global__ void __launch_bounds__(256) k_hash_ids(const void* x, int B, int head
 // ---------------------------------------------------------------------------
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-size_t graph_workspace_layout(const GraphShape& s, GraphDev* g) {
-  const int64_t BG = (int64_t)s.B * s.n_kv;
-  const int64_t W = ((s.M + 63) / 64 + 1) / 2 * 2;  // padded to an even word count
-  const int64_t NB = int64_t(1) << s.p;
+size_t graph_workspace_layout(GraphDev* g) {
+  const int64_t BG = (int64_t)g->B * g->n_kv;
+  const int64_t W = g->Wpad;
+  const int64_t NB = int64_t(1) << g->p;
+  const int64_t rows = (int64_t)g->B * g->H * g->N;
+  g->capg = ((4 * g->A + 64) + 7) / 8 * 8;
+  g->sample_s = g->A / 12 > 1 ? g->A / 12 : 1;
+  g->use_tc = select_tc_supported(*g) ? 1 : 0;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
     off = align256(off + bytes);
     return o;
   };
-  const size_t o_kcode = take(sizeof(uint16_t) * BG * s.R * s.M);
+  const size_t o_kcode = take(sizeof(uint16_t) * BG * g->R * g->M);
   const size_t o_zero_begin = off;
-  const size_t o_bmap = take(sizeof(unsigned long long) * BG * W * s.R * NB);
+  const size_t o_bmap = take(sizeof(unsigned long long) * BG * W * g->R * NB);
   const size_t o_pmask = take(sizeof(unsigned long long) * BG * W);
-  const size_t o_pmax = take(sizeof(uint32_t) * BG * s.R);
+  const size_t o_pmax = take(sizeof(uint32_t) * BG * g->R);
+  const int64_t ntq = (g->N + 127) / 128;
+  const size_t o_flags = take((size_t)g->B * g->H * ntq);
   const size_t o_zero_end = off;
-  const size_t o_bsize = take(sizeof(int32_t) * BG * s.R * NB);
-  const size_t o_lastc = take(sizeof(int32_t) * BG * s.R * NB);
-  const size_t o_lsh = s.need_lsh_scratch ? take(sizeof(int32_t) * (size_t)s.B * s.H * s.N * s.A) : 0;
-  if (g) {
+  const size_t o_bsize = take(sizeof(int32_t) * BG * g->R * NB);
+  const size_t o_lastc = take(sizeof(int32_t) * BG * g->R * NB);
+  size_t o_qids = 0, o_qempty = 0, o_tau = 0, o_rcnt = 0, o_bufs = 0, o_bufk = 0;
+  if (g->use_tc) {
+    o_qids = take(sizeof(uint16_t) * rows * g->NT);
+    o_qempty = take(rows);
+    o_tau = take(sizeof(float) * rows);
+    o_rcnt = take(sizeof(int32_t) * rows);
+    o_bufs = take(sizeof(float) * rows * g->capg);
+    o_bufk = take(sizeof(uint16_t) * rows * g->capg);
+  }
+  if (g->ws) {
     char* base = static_cast<char*>(g->ws);
     g->kcode = reinterpret_cast<uint16_t*>(base + o_kcode);
     g->bmap = reinterpret_cast<unsigned long long*>(base + o_bmap);
     g->pmask = reinterpret_cast<unsigned long long*>(base + o_pmask);
     g->pmax = reinterpret_cast<uint32_t*>(base + o_pmax);
+    g->tile_flags = reinterpret_cast<uint8_t*>(base + o_flags);
     g->bsize = reinterpret_cast<int32_t*>(base + o_bsize);
     g->lastc = reinterpret_cast<int32_t*>(base + o_lastc);
-    if (s.need_lsh_scratch) g->lsh = reinterpret_cast<int32_t*>(base + o_lsh);
+    if (g->use_tc) {
+      g->qids = reinterpret_cast<uint16_t*>(base + o_qids);
+      g->qempty = reinterpret_cast<uint8_t*>(base + o_qempty);
+      g->tau = reinterpret_cast<float*>(base + o_tau);
+      g->rcnt = reinterpret_cast<int32_t*>(base + o_rcnt);
+      g->bufs = reinterpret_cast<float*>(base + o_bufs);
+      g->bufk = reinterpret_cast<uint16_t*>(base + o_bufk);
+    }
     g->zero_off = o_zero_begin;
     g->zero_bytes = o_zero_end - o_zero_begin;
   }
@@ -460,12 +484,18 @@ cudaError_t launch_graph(const GraphDev& g, int mode, cudaStream_t st) {
   }
   k_bucket_trim<<<g.B * g.n_kv * g.R, 256, 0, st>>>(g);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  if (select_tc_supported(g)) return launch_select_tc(g, mode, st);
+  GraphDev f = g;
+  if (g.use_tc && select_tc_pointers_ok(g)) {
+    if ((e = launch_select_tc(g, mode, st)) != cudaSuccess) return e;
+    f.fallback_only = 1;  // exact FMA scan for the tiles the selection flagged
+  } else {
+    f.fallback_only = 0;
+  }
   int rows;
   size_t smem;
-  if (choose_select_rows(g, &rows, &smem)) return cudaErrorInvalidConfiguration;
-  return g.dtype == kDtF32 ? launch_select_dt<kDtF32>(g, mode, rows, smem, st)
-                           : launch_select_dt<kDtBF16>(g, mode, rows, smem, st);
+  if (choose_select_rows(f, &rows, &smem)) return cudaErrorInvalidConfiguration;
+  return f.dtype == kDtF32 ? launch_select_dt<kDtF32>(f, mode, rows, smem, st)
+                           : launch_select_dt<kDtBF16>(f, mode, rows, smem, st);
 }
 
 cudaError_t launch_merge(const MergeDev& m, cudaStream_t st) {

@@ -8,10 +8,6 @@
 
 namespace ssa {
 
-struct GraphShape {
-  int B, H, n_kv, N, M, d, R, p, A;
-  bool need_lsh_scratch;
-};
 
 // Everything a graph-build kernel needs, passed by value.
 struct GraphDev {
@@ -32,17 +28,32 @@ struct GraphDev {
   uint32_t* pmax;                 // [BG][R] (bucket << 20 | key) of perm_r[M-1]
   int32_t* bsize;                 // [BG][R][NB]
   int32_t* lastc;                 // [BG][R][NB] key at rank min(size, C) - 1
+  // tensor-core path (bf16): per query row
+  int use_tc, capg, sample_s, fallback_only;
+  uint16_t* qids;                 // [B*H*N][NT] bucket id per (round, probe) slot
+  uint8_t* qempty;                // [B*H*N] some slot's bucket is empty
+  float* tau;                     // [B*H*N] scan threshold
+  int32_t* rcnt;                  // [B*H*N] kept candidates (> capg: overflow)
+  float* bufs;                    // [B*H*N][capg] kept scores
+  uint16_t* bufk;                 // [B*H*N][capg] kept keys
+  uint8_t* tile_flags;            // [B*H][ceil(N/128)] tiles for the exact fallback
   // outputs
   int32_t* lsh;                   // [B][H][N][A]
   int32_t* nb;                    // [B][H][N][Wout]
   uint8_t* valid;                 // [B][H][N][Wout]
 };
 
-size_t graph_workspace_layout(const GraphShape& s, GraphDev* g);
+// Fills the workspace pointers of g (g->ws may be null to only size it) and
+// returns the bytes needed. Decides g->use_tc from the shapes.
+size_t graph_workspace_layout(GraphDev* g);
 int choose_select_rows(const GraphDev& g, int* rows_out, size_t* smem_out);
 cudaError_t launch_graph(const GraphDev& g, int mode, cudaStream_t st);
 bool select_tc_supported(const GraphDev& g);
+bool select_tc_pointers_ok(const GraphDev& g);
 cudaError_t launch_select_tc(const GraphDev& g, int mode, cudaStream_t st);
+cudaError_t launch_hash_queries(const GraphDev& g, cudaStream_t st);
+cudaError_t launch_rows(const GraphDev& g, int stage, int mode, cudaStream_t st);
+size_t rows_smem_bytes(const GraphDev& g, int warps);
 int read_device_error(int clear);
 struct MergeDev {
   int B, H, N, A, Kw, G, Wout;

@@ -33,7 +33,6 @@ namespace tc {
 
 constexpr int ROWS = 128;   // query rows per CTA (MMA M, TMEM lanes)
 constexpr int NKEY = 128;   // keys per tile (MMA N)
-constexpr int STAGES = 2;   // K-tile ring
 constexpr int THREADS = 192;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -69,10 +68,10 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
 // Bounded wait: about a few seconds at most, then flag the error.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           int code) {
-  for (uint32_t i = 0; i < (1u << 22); ++i) {
+  for (uint32_t i = 0; i < (1u << 24); ++i) {
     if (mbar_try(bar, parity)) return true;
     if (*abort) return false;
-    if (i > 64) __nanosleep(256);
+    if (i > 2048) __nanosleep(64);
   }
   *abort = 1;
   atomicCAS(&g_ssa_device_error, 0, code);
@@ -90,9 +89,9 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, v
 // Bounded wait that ignores the abort flag: used to let TMA copies already
 // issued land before the CTA exits.
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < (1u << 22); ++i) {
+  for (uint32_t i = 0; i < (1u << 24); ++i) {
     if (mbar_try(bar, parity)) return;
-    if (i > 64) __nanosleep(256);
+    if (i > 2048) __nanosleep(64);
   }
   atomicCAS(&g_ssa_device_error, 0, 17);
 }
@@ -160,11 +159,27 @@ __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// a[j] for a dynamic j in [0, 32) without indexing the register array
+// (which would move it to local memory): a 5-level select tree.
+__device__ __forceinline__ float pick32(const float* a, int j) {
+  float b16[16], b8[8], b4[4], b2[2];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) b16[i] = (j & 16) ? a[i + 16] : a[i];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) b8[i] = (j & 8) ? b16[i + 8] : b16[i];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) b4[i] = (j & 4) ? b8[i + 4] : b8[i];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) b2[i] = (j & 2) ? b4[i + 2] : b4[i];
+  return (j & 1) ? b2[1] : b2[0];
+}
+
 struct SmemPlan {
-  uint32_t q, k, heap_s, heap_k, tids, gs, bars, tmem_slot, total;
+  uint32_t q, k, tids, bars, tmem_slot, total;
+  int stages;
 };
 
-__host__ __device__ inline SmemPlan plan(int D, int A, int NT, int G, int key_bytes) {
+__host__ __device__ inline SmemPlan plan_stages(int D, int NT, int stages) {
   SmemPlan p;
   uint32_t off = 0;
   auto take = [&](uint32_t bytes, uint32_t align) {
@@ -175,42 +190,56 @@ __host__ __device__ inline SmemPlan plan(int D, int A, int NT, int G, int key_by
   };
   const uint32_t atoms = (uint32_t)D / 64;
   p.q = take(atoms * ROWS * 128, 1024);
-  p.k = take(STAGES * atoms * NKEY * 128, 1024);
-  p.heap_s = take((uint32_t)A * ROWS * 4, 16);
-  p.heap_k = take((uint32_t)A * ROWS * key_bytes, 16);
+  p.k = take((uint32_t)stages * atoms * NKEY * 128, 1024);
   p.tids = take((uint32_t)NT * ROWS * 2, 16);
-  p.gs = take((uint32_t)(G + 1) * 4, 16);
   p.bars = take(16 * 8, 8);
   p.tmem_slot = take(16, 16);
-  p.total = off + 1024;  // slack to realign the dynamic base to 1024 bytes
+  // At least 80 KB per CTA so that at most two CTAs share an SM: two CTAs
+  // use all 512 TMEM columns, a third would wait in tcgen05.alloc.
+  uint32_t total = off + 1024;
+  if (total < 80 * 1024) total = 80 * 1024;
+  p.total = total;
+  p.stages = stages;
   return p;
+}
+
+// The deepest K ring (up to 4 stages) that keeps two CTAs per SM.
+__host__ __device__ inline SmemPlan plan(int D, int NT) {
+  for (int st = 4; st > 2; --st) {
+    const SmemPlan p = plan_stages(D, NT, st);
+    if (p.total <= 113 * 1024) return p;
+  }
+  return plan_stages(D, NT, 2);
 }
 
 }  // namespace tc
 
-template <int D, typename KT>
-__global__ void __launch_bounds__(tc::THREADS, 1)
-    k_select_tc(GraphDev g, int mode, const __grid_constant__ CUtensorMap qmap,
-                const __grid_constant__ CUtensorMap kmap) {
+// Candidate scan. pass 0 (sample): key tiles 0, s, 2s, ... and every
+// candidate is kept; pass 1 (full): all key tiles, candidates with
+// score >= tau[row] are kept. Kept (score, key) pairs go to the row's slice of
+// the global buffer; the row's count goes to rcnt (a count above the buffer
+// capacity means overflow).
+template <int D>
+__global__ void __launch_bounds__(tc::THREADS, 2)
+    k_scan_tc(GraphDev g, int pass, const __grid_constant__ CUtensorMap qmap,
+              const __grid_constant__ CUtensorMap kmap) {
   using namespace tc;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int ATOMS = D / 64;
-  const SmemPlan sp = plan(D, g.A, g.NT, g.G, (int)sizeof(KT));
+  const SmemPlan sp = plan(D, g.NT);
+  const int NS = sp.stages;
   unsigned char* qs = smem + sp.q;
   unsigned char* ks = smem + sp.k;
-  float* hs = reinterpret_cast<float*>(smem + sp.heap_s);
-  KT* hk = reinterpret_cast<KT*>(smem + sp.heap_k);
   uint16_t* tids = reinterpret_cast<uint16_t*>(smem + sp.tids);
-  int32_t* gs = reinterpret_cast<int32_t*>(smem + sp.gs);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + sp.bars);
-  uint64_t* kfull = bars;           // [2] K stage loaded (TMA tx)
-  uint64_t* kempty = bars + 2;      // [2] K stage consumed (MMA commit)
-  uint64_t* sfull = bars + 4;       // [2] S accumulator ready (MMA commit)
-  uint64_t* sempty = bars + 6;      // [2] S accumulator drained (4 epilogue warps)
-  uint64_t* qfull = bars + 8;       // q tile loaded
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 9);
+  uint64_t* kfull = bars;           // [NS] K stage loaded (TMA tx)
+  uint64_t* kempty = bars + 4;      // [NS] K stage consumed (MMA commit)
+  uint64_t* sfull = bars + 8;       // [2] S accumulator ready (MMA commit)
+  uint64_t* sempty = bars + 10;     // [2] S accumulator drained (4 epilogue warps)
+  uint64_t* qfull = bars + 12;      // q tile loaded
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 13);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + sp.tmem_slot);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -220,31 +249,22 @@ __global__ void __launch_bounds__(tc::THREADS, 1)
   const int bg = b * g.n_kv + gk;
   const int n0 = blockIdx.x * ROWS;
   const int n_hi = min(g.N, n0 + ROWS) - 1;
-  const int nkt = g.causal ? min((g.M + NKEY - 1) / NKEY, (n_hi >> 7) + 1) : (g.M + NKEY - 1) / NKEY;
+  const int nkt_all = g.causal ? min((g.M + NKEY - 1) / NKEY, (n_hi >> 7) + 1) : (g.M + NKEY - 1) / NKEY;
+  const int step = pass == 0 ? g.sample_s : 1;
+  const int ntl = (nkt_all + step - 1) / step;  // tiles this CTA visits: 0, step, 2*step, ...
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(kfull + i, 1);
       mbar_init(kempty + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(sfull + i, 1);
       mbar_init(sempty + i, 4);
     }
     mbar_init(qfull, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    // sorted unique globals for the merge
-    int ng = 0;
-    for (int i = 0; i < g.G; ++i) {
-      const int v = g.glob[i];
-      bool dup = false;
-      for (int z = 0; z < ng; ++z) dup |= gs[z] == v;
-      if (dup) continue;
-      int j = ng - 1;
-      while (j >= 0 && gs[j] > v) { gs[j + 1] = gs[j]; --j; }
-      gs[j + 1] = v;
-      ++ng;
-    }
-    gs[g.G] = ng;
   }
   if (warp == 5) {  // TMEM: 2 accumulators x NKEY fp32 columns
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -264,37 +284,36 @@ __global__ void __launch_bounds__(tc::THREADS, 1)
       for (int a = 0; a < ATOMS; ++a)
         tma_load_4d(qs + a * ROWS * 128, &qmap, qfull, a * 64, h, n0, b);
       int issued = 0;
-      for (int kt = 0; kt < nkt; ++kt) {
-        const int s = kt & 1;
-        if (!mbar_wait(kempty + s, ((kt >> 1) & 1) ^ 1, abort_flag, 11)) break;
+      for (int i = 0; i < ntl; ++i) {
+        const int s = i % NS;
+        if (!mbar_wait(kempty + s, ((i / NS) & 1) ^ 1, abort_flag, 11)) break;
         mbar_expect_tx(kfull + s, ATOMS * NKEY * 128);
         for (int a = 0; a < ATOMS; ++a)
-          tma_load_4d(ks + (s * ATOMS + a) * NKEY * 128, &kmap, kfull + s, a * 64, gk, kt * NKEY, b);
-        issued = kt + 1;
+          tma_load_4d(ks + (s * ATOMS + a) * NKEY * 128, &kmap, kfull + s, a * 64, gk, i * step * NKEY, b);
+        issued = i + 1;
       }
-      // Do not leave while copies are in flight: the last two issued stages
-      // (and the q tile) must have landed before the CTA's shared memory goes.
+      // Do not leave while copies are in flight.
       mbar_drain(qfull, 0);
-      for (int kt = max(0, issued - 2); kt < issued; ++kt) mbar_drain(kfull + (kt & 1), (kt >> 1) & 1);
+      for (int i = max(0, issued - NS); i < issued; ++i) mbar_drain(kfull + i % NS, (i / NS) & 1);
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && mbar_wait(qfull, 0, abort_flag, 13)) {
       const uint32_t qa = smem_u32(qs);
-      for (int kt = 0; kt < nkt; ++kt) {
-        const int s = kt & 1;
-        if (!mbar_wait(kfull + s, (kt >> 1) & 1, abort_flag, 14)) break;
-        if (!mbar_wait(sempty + s, ((kt >> 1) & 1) ^ 1, abort_flag, 15)) break;
+      for (int i = 0; i < ntl; ++i) {
+        const int s = i % NS, sb = i & 1;
+        if (!mbar_wait(kfull + s, (i / NS) & 1, abort_flag, 14)) break;
+        if (!mbar_wait(sempty + sb, ((i >> 1) & 1) ^ 1, abort_flag, 15)) break;
         tc_fence_after();
         const uint32_t ka = smem_u32(ks + s * ATOMS * NKEY * 128);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (ROWS * 128) + (kk & 3) * 32;
           const uint32_t offk = (kk >> 2) * (NKEY * 128) + (kk & 3) * 32;
-          umma_bf16(tmem + s * NKEY, umma_desc(qa + off), umma_desc(ka + offk), kk > 0);
+          umma_bf16(tmem + sb * NKEY, umma_desc(qa + off), umma_desc(ka + offk), kk > 0);
         }
         umma_commit(kempty + s);
-        umma_commit(sfull + s);
+        umma_commit(sfull + sb);
       }
     }
     __syncwarp();
@@ -303,73 +322,76 @@ __global__ void __launch_bounds__(tc::THREADS, 1)
     const int t = threadIdx.x;  // row within the tile; TMEM lane
     const int n = n0 + t;
     const bool act = n < g.N;
-    bool any_empty = false;
-    if (act) {
-      float q[D];
-      const void* qrow = row_ptr<kDtBF16>(g.q, b * g.q_sb + h * g.q_sh + (int64_t)n * g.q_sn);
-#pragma unroll
-      for (int i = 0; i < D; i += 4) {
-        const float4 x = load4<kDtBF16>(qrow, i);
-        q[i] = x.x; q[i + 1] = x.y; q[i + 2] = x.z; q[i + 3] = x.w;
-      }
-      any_empty = hash_row_ids<D>(g, q, bg, tids, ROWS, t);
-    }
-    RowHeap<KT> heap{hs, hk, ROWS, t};
+    const int64_t row = (int64_t)bh * g.N + n;
+    if (act)
+      for (int tt = 0; tt < g.NT; ++tt) tids[tt * ROWS + t] = g.qids[row * g.NT + tt];
+    const float thr = (pass == 1 && act) ? g.tau[row] : -INFINITY;
+    float* bs = g.bufs + row * g.capg;
+    uint16_t* bk = g.bufk + row * g.capg;
     int cnt = 0;
-    float thr = -INFINITY;
     const unsigned long long* bmg = g.bmap + (int64_t)bg * g.Wpad * g.R * g.NB;
-    for (int kt = 0; kt < nkt; ++kt) {
-      const int s = kt & 1;
-      if (!mbar_wait_warp(sfull + s, (kt >> 1) & 1, abort_flag, 16)) break;
-      tc_fence_after();
-      float sc[NKEY];
-      const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + s * NKEY;
-#pragma unroll
-      for (int c = 0; c < NKEY / 32; ++c) tmem_ld32(ta + c * 32, sc + c * 32);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(sempty + s);
-      if (!act) continue;
+    for (int i = 0; i < ntl; ++i) {
+      const int sb = i & 1;
+      const int kt = i * step;
       const int key0 = kt * NKEY;
-      unsigned long long w[2];
+      // Candidate masks first: their loads overlap the wait for S.
+      unsigned long long w[2] = {0ull, 0ull};
+      if (act) {
 #pragma unroll
-      for (int hw = 0; hw < 2; ++hw) {
-        const unsigned long long* bm = bmg + (int64_t)(2 * kt + hw) * g.R * g.NB;
-        unsigned long long x = 0ull;
-        for (int tt = 0; tt < g.NT; ++tt) x |= __ldg(bm + (tt / (1 + g.Te)) * g.NB + tids[tt * ROWS + t]);
-        x &= ~__ldg(g.pmask + (int64_t)bg * g.Wpad + 2 * kt + hw);
-        if (g.causal) {
-          const int lim = n - (key0 + 64 * hw);
-          if (lim <= 0) x = 0ull;
-          else if (lim < 64) x &= (1ull << lim) - 1ull;
+        for (int hw = 0; hw < 2; ++hw) {
+          const unsigned long long* bm = bmg + (int64_t)(2 * kt + hw) * g.R * g.NB;
+          unsigned long long x = 0ull;
+          for (int tt = 0; tt < g.NT; ++tt)
+            x |= __ldg(bm + (tt / (1 + g.Te)) * g.NB + tids[tt * ROWS + t]);
+          x &= ~__ldg(g.pmask + (int64_t)bg * g.Wpad + 2 * kt + hw);
+          if (g.causal) {
+            const int lim = n - (key0 + 64 * hw);
+            if (lim <= 0) x = 0ull;
+            else if (lim < 64) x &= (1ull << lim) - 1ull;
+          }
+          w[hw] = x;
         }
-        w[hw] = x;
       }
+      if (!mbar_wait_warp(sfull + sb, (i >> 1) & 1, abort_flag, 16)) break;
+      tc_fence_after();
+      const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + sb * NKEY;
 #pragma unroll
       for (int hw = 0; hw < 2; ++hw) {
-        const unsigned long long x = w[hw];
-        if (!x) continue;
+        float sc[64];
+        tmem_ld32(ta + hw * 64, sc);
+        tmem_ld32(ta + hw * 64 + 32, sc + 32);
+        tmem_wait_ld();
+        if (hw == 1) {  // the accumulator can be reused once both halves are read
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(sempty + sb);
+        }
 #pragma unroll
-        for (int j = 0; j < 64; ++j) {
-          const float v = sc[hw * 64 + j];
-          if (((x >> j) & 1ull) && v > thr) {
-            if (cnt < g.A) {
-              heap.set(cnt, v, key0 + hw * 64 + j);
-              if (++cnt == g.A) {
-                heap.heapify_score(g.A);
-                thr = heap.sc(0);
-              }
-            } else {
-              heap.sift_score(0, g.A, v, key0 + hw * 64 + j);
-              thr = heap.sc(0);
+        for (int c = 0; c < 2; ++c) {
+          const uint32_t cm = (uint32_t)(w[hw] >> (c * 32));
+          if (!cm) continue;
+          uint32_t h0 = 0, h1 = 0, h2 = 0, h3 = 0;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            h0 |= (sc[c * 32 + j] >= thr ? 1u : 0u) << j;
+            h1 |= (sc[c * 32 + j + 1] >= thr ? 2u : 0u) << j;
+            h2 |= (sc[c * 32 + j + 2] >= thr ? 4u : 0u) << j;
+            h3 |= (sc[c * 32 + j + 3] >= thr ? 8u : 0u) << j;
+          }
+          uint32_t hit = (h0 | h1 | h2 | h3) & cm;
+          while (hit) {
+            const int j = __ffs(hit) - 1;
+            hit &= hit - 1;
+            if (cnt < g.capg) {
+              bs[cnt] = pick32(sc + c * 32, j);
+              bk[cnt] = (uint16_t)(key0 + hw * 64 + c * 32 + j);
             }
+            ++cnt;
           }
         }
       }
     }
-    if (act && !*abort_flag) finish_row<kDtBF16, D, KT>(g, mode, heap, cnt, tids, ROWS, t, gs, bh, b, h,
-                                                        gk, bg, n, any_empty);
+    if (act) g.rcnt[row] = cnt;
   }
   tc_fence_before();
   __syncthreads();
@@ -416,34 +438,48 @@ static bool make_map(CUtensorMap* m, const void* base, int d, int heads, int row
 
 bool select_tc_supported(const GraphDev& g) {
   if (g.dtype != kDtBF16 || (g.d != 64 && g.d != 128)) return false;
-  // TMA: 16-byte aligned base and strides
+  if (g.M > 65536 || g.A > 1024) return false;
+  // TMA: 16-byte aligned strides (the base pointers are checked at launch)
   auto al = [](int64_t s) { return (s * 2) % 16 == 0; };
   if (!al(g.q_sh) || !al(g.q_sn) || !al(g.q_sb) || !al(g.k_sh) || !al(g.k_sm) || !al(g.k_sb)) return false;
-  if ((reinterpret_cast<uintptr_t>(g.q) % 16) || (reinterpret_cast<uintptr_t>(g.k) % 16)) return false;
-  const tc::SmemPlan sp = tc::plan(g.d, g.A, g.NT, g.G, g.M <= 65536 ? 2 : 4);
-  if (sp.total > 227 * 1024) return false;
+  const tc::SmemPlan sp = tc::plan(g.d, g.NT);
+  if (sp.total > 113 * 1024) return false;
+  if (rows_smem_bytes(g, 1) > 227 * 1024) return false;
   return encode_fn() != nullptr;
 }
 
-template <int D, typename KT>
-static cudaError_t launch_tc_t(const GraphDev& g, int mode, cudaStream_t st) {
+bool select_tc_pointers_ok(const GraphDev& g) {
+  return (reinterpret_cast<uintptr_t>(g.q) % 16) == 0 && (reinterpret_cast<uintptr_t>(g.k) % 16) == 0;
+}
+
+template <int D>
+static cudaError_t launch_scan_t(const GraphDev& g, int pass, const CUtensorMap& qmap,
+                                 const CUtensorMap& kmap, cudaStream_t st) {
+  const tc::SmemPlan sp = tc::plan(D, g.NT);
+  auto fn = k_scan_tc<D>;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp.total);
+  if (e != cudaSuccess) return e;
+  dim3 grid((g.N + tc::ROWS - 1) / tc::ROWS, g.B * g.H);
+  fn<<<grid, tc::THREADS, sp.total, st>>>(g, pass, qmap, kmap);
+  return cudaGetLastError();
+}
+
+// hash queries -> sample scan -> thresholds -> full scan -> exact selection
+// (+ merge). Rows flagged by the selection are recomputed afterwards by the
+// exact FMA scan (launch_graph).
+cudaError_t launch_select_tc(const GraphDev& g, int mode, cudaStream_t st) {
   CUtensorMap qmap, kmap;
   // q (B, H, N, d): dims {d, H, N, B}; k (B, n_kv, M, d): dims {d, n_kv, M, B}
   if (!make_map(&qmap, g.q, g.d, g.H, g.N, g.B, g.q_sh, g.q_sn, g.q_sb)) return cudaErrorInvalidValue;
   if (!make_map(&kmap, g.k, g.d, g.n_kv, g.M, g.B, g.k_sh, g.k_sm, g.k_sb)) return cudaErrorInvalidValue;
-  const tc::SmemPlan sp = tc::plan(D, g.A, g.NT, g.G, (int)sizeof(KT));
-  auto fn = k_select_tc<D, KT>;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp.total);
-  if (e != cudaSuccess) return e;
-  dim3 grid((g.N + tc::ROWS - 1) / tc::ROWS, g.B * g.H);
-  fn<<<grid, tc::THREADS, sp.total, st>>>(g, mode, qmap, kmap);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_select_tc(const GraphDev& g, int mode, cudaStream_t st) {
-  const bool k16 = g.M <= 65536;
-  if (g.d == 64) return k16 ? launch_tc_t<64, uint16_t>(g, mode, st) : launch_tc_t<64, uint32_t>(g, mode, st);
-  return k16 ? launch_tc_t<128, uint16_t>(g, mode, st) : launch_tc_t<128, uint32_t>(g, mode, st);
+  cudaError_t e;
+  if ((e = launch_hash_queries(g, st)) != cudaSuccess) return e;
+  for (int pass = 0; pass < 2; ++pass) {
+    e = g.d == 64 ? launch_scan_t<64>(g, pass, qmap, kmap, st) : launch_scan_t<128>(g, pass, qmap, kmap, st);
+    if (e != cudaSuccess) return e;
+    if ((e = launch_rows(g, pass, mode, st)) != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 int read_device_error(int clear) {
