@@ -367,7 +367,7 @@ size_t graph_workspace_layout(GraphDev* g) {
   const int64_t W = g->Wpad;
   const int64_t NB = int64_t(1) << g->p;
   const int64_t rows = (int64_t)g->B * g->H * g->N;
-  g->capg = ((4 * g->A + 64) + 7) / 8 * 8;
+  g->capg = ((6 * g->A + 64) + 7) / 8 * 8;
   g->sample_s = g->A / 12 > 1 ? g->A / 12 : 1;
   g->use_tc = select_tc_supported(*g) ? 1 : 0;
   size_t off = 0;
@@ -386,14 +386,13 @@ size_t graph_workspace_layout(GraphDev* g) {
   const size_t o_zero_end = off;
   const size_t o_bsize = take(sizeof(int32_t) * BG * g->R * NB);
   const size_t o_lastc = take(sizeof(int32_t) * BG * g->R * NB);
-  size_t o_qids = 0, o_qempty = 0, o_tau = 0, o_rcnt = 0, o_bufs = 0, o_bufk = 0;
+  size_t o_qids = 0, o_qempty = 0, o_tau = 0, o_rcnt = 0, o_buf = 0;
   if (g->use_tc) {
     o_qids = take(sizeof(uint16_t) * rows * g->NT);
     o_qempty = take(rows);
     o_tau = take(sizeof(float) * rows);
     o_rcnt = take(sizeof(int32_t) * rows);
-    o_bufs = take(sizeof(float) * rows * g->capg);
-    o_bufk = take(sizeof(uint16_t) * rows * g->capg);
+    o_buf = take(sizeof(unsigned long long) * rows * g->capg);
   }
   if (g->ws) {
     char* base = static_cast<char*>(g->ws);
@@ -409,8 +408,7 @@ size_t graph_workspace_layout(GraphDev* g) {
       g->qempty = reinterpret_cast<uint8_t*>(base + o_qempty);
       g->tau = reinterpret_cast<float*>(base + o_tau);
       g->rcnt = reinterpret_cast<int32_t*>(base + o_rcnt);
-      g->bufs = reinterpret_cast<float*>(base + o_bufs);
-      g->bufk = reinterpret_cast<uint16_t*>(base + o_bufk);
+      g->buf = reinterpret_cast<unsigned long long*>(base + o_buf);
     }
     g->zero_off = o_zero_begin;
     g->zero_bytes = o_zero_end - o_zero_begin;

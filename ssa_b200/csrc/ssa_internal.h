@@ -34,8 +34,7 @@ struct GraphDev {
   uint8_t* qempty;                // [B*H*N] some slot's bucket is empty
   float* tau;                     // [B*H*N] scan threshold
   int32_t* rcnt;                  // [B*H*N] kept candidates (> capg: overflow)
-  float* bufs;                    // [B*H*N][capg] kept scores
-  uint16_t* bufk;                 // [B*H*N][capg] kept keys
+  unsigned long long* buf;        // [B*H*N][capg] kept (key << 32 | score bits)
   uint8_t* tile_flags;            // [B*H][ceil(N/128)] tiles for the exact fallback
   // outputs
   int32_t* lsh;                   // [B][H][N][A]

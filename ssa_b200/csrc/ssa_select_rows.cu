@@ -163,17 +163,19 @@ __global__ void __launch_bounds__(256) k_rows(GraphDev g, int stage, int mode) {
     const int bg = b * g.n_kv + gk;
     const int cnt_all = g.rcnt[row];
     const int c = min(cnt_all, g.capg);
-    const float* bs = g.bufs + row * g.capg;
-    const uint16_t* bk = g.bufk + row * g.capg;
+    const unsigned long long* bo = g.buf + row * g.capg;
     if (stage == 0) {
       // ---- THRESH: tau = x-th largest sampled score ----------------------
       const int tiles_row = g.causal ? (n + 127) / 128 : (g.M + 127) / 128;
       const int sampled = tiles_row > 0 ? (tiles_row + g.sample_s - 1) / g.sample_s : 0;
       float tau = -INFINITY;
       if (sampled > 0 && tiles_row > 0) {
-        const int x = (int)(((int64_t)2 * g.A * sampled + tiles_row - 1) / tiles_row);
+        // x ~ 3A scaled by the sampled fraction: about 3A candidates are
+        // expected at or above tau, so fewer than A (the fallback case) is
+        // a 3x deviation, and more than the buffer holds (6A+64) a 2x one.
+        const int x = (int)(((int64_t)3 * g.A * sampled + tiles_row - 1) / tiles_row);
         if (x >= 1 && c >= x) {
-          for (int i = lane; i < c; i += 32) S.sc[i] = bs[i];
+          for (int i = lane; i < c; i += 32) S.sc[i] = __uint_as_float((uint32_t)bo[i]);
           __syncwarp();
           int need;
           const uint32_t T = warp_radix_kth(S.sc, c, x, S.hist, &need);
@@ -193,31 +195,39 @@ __global__ void __launch_bounds__(256) k_rows(GraphDev g, int stage, int mode) {
       continue;
     }
     for (int i = lane; i < c; i += 32) {
-      S.sc[i] = bs[i];
-      S.ky[i] = bk[i];
+      const unsigned long long e = bo[i];
+      S.sc[i] = __uint_as_float((uint32_t)e);
+      S.ky[i] = (int32_t)(e >> 32);
     }
     // Special keys: pad keys perm_r[M-1], causal self, empty-bucket fallbacks.
     const bool any_empty = g.qempty[row] != 0;
     const int lim_g = g.G < g.C ? g.G : g.C;
-    int nspec = 0;
-    if (lane == 0) {
-      auto add = [&](int x) {
-        if (x < 0 || x >= g.M) return;
-        for (int z = 0; z < nspec; ++z)
-          if (S.spec[z] == x) return;
-        if (nspec < 64) S.spec[nspec++] = x;
-      };
-      for (int r = 0; r < g.R; ++r) {
-        const int P = (int)(g.pmax[bg * g.R + r] & 0xFFFFFu);
-        if (!(g.causal && P > n)) add(P);
-      }
-      if (g.causal) add(n);
-      if (any_empty) {
-        for (int i = 0; i < lim_g; ++i) add(g.glob[i]);
-        if (g.G < g.C) add(0);
-      }
+    // Candidate list at fixed positions, one per lane (the tensor-core path
+    // requires R + min(G, C) + 2 <= 32): R pad keys, causal self, and (only if
+    // a bucket of this row is empty) the fallback globals and key 0. A lane
+    // keeps its entry unless it is out of range or repeats an earlier one;
+    // kept entries are compacted in order.
+    const int ncand = g.R + 1 + (any_empty ? lim_g + 1 : 0);
+    int x = -1;
+    if (lane < g.R) {
+      x = (int)(g.pmax[bg * g.R + lane] & 0xFFFFFu);
+      if (g.causal && x > n) x = -1;  // a future pad key never appears as itself
+    } else if (lane == g.R) {
+      x = g.causal ? n : -1;
+    } else if (lane < ncand - 1) {
+      x = g.glob[lane - g.R - 1];
+    } else if (lane == ncand - 1 && any_empty) {
+      x = g.G < g.C ? 0 : -1;
     }
-    nspec = __shfl_sync(0xffffffffu, nspec, 0);
+    if (x >= g.M) x = -1;
+    bool keep = x >= 0;
+    for (int z = 0; z < 32; ++z) {
+      const int y = __shfl_sync(0xffffffffu, x, z);
+      if (z < lane && y == x) keep = false;
+    }
+    const unsigned km = __ballot_sync(0xffffffffu, keep);
+    if (keep) S.spec[__popc(km & ((1u << lane) - 1u))] = x;
+    const int nspec = __popc(km);
     __syncwarp();
     const uint16_t* tids = g.qids + row * g.NT;
     // Replay, lane-parallel over (key, slot) pairs: flag 1 = key's slot in
@@ -229,7 +239,15 @@ __global__ void __launch_bounds__(256) k_rows(GraphDev g, int stage, int mode) {
       const int x = S.spec[i];
       const int r = tt / (1 + g.Te);
       const int u = tids[tt];
-      const int sz = g.bsize[(bg * g.R + r) * g.NB + u];
+      // every load issued up front (no dependent chain)
+      const int64_t tb = (int64_t)(bg * g.R + r) * g.NB + u;
+      const int sz = __ldg(g.bsize + tb);
+      const int lc = __ldg(g.lastc + tb);
+      const uint32_t pm = __ldg(g.pmax + bg * g.R + r);
+      const uint16_t code = __ldg(g.kcode + ((int64_t)bg * g.R + r) * g.M + x);
+      const unsigned long long wbits =
+          __ldg(&g.bmap[(((int64_t)bg * g.Wpad + (x >> 6)) * g.R + r) * g.NB + u]);
+      const bool member = code == (uint16_t)u && ((wbits >> (x & 63)) & 1ull);
       uint8_t f = 0;
       if (sz == 0) {
         bool in = false;
@@ -239,11 +257,11 @@ __global__ void __launch_bounds__(256) k_rows(GraphDev g, int stage, int mode) {
       } else {
         bool real;
         if (g.causal && x > n) real = false;
-        else if (g.causal && x == n) real = g.lastc[(bg * g.R + r) * g.NB + u] > n || key_member(g, bg, r, u, n);
-        else real = key_member(g, bg, r, u, x);
+        else if (g.causal && x == n) real = lc > n || member;
+        else real = member;
         if (real) f = 1;
         else if (sz < g.C) {
-          int P = (int)(g.pmax[bg * g.R + r] & 0xFFFFFu);
+          int P = (int)(pm & 0xFFFFFu);
           if (g.causal && P > n) P = n;
           if (P == x) f = 2;
         }
@@ -382,7 +400,7 @@ __global__ void __launch_bounds__(256) k_rows(GraphDev g, int stage, int mode) {
       atomicOr(&S.bits[idx >> 5], 1u << (idx & 31));
     }
     for (int j = lane; j < g.G; j += 32) {
-      const int x = g.glob[j];
+      const int x = min(max(g.glob[j], 0), g.M - 1);
       atomicOr(&S.bits[x >> 5], 1u << (x & 31));
     }
     if (add_zero && lane == 0) atomicOr(&S.bits[0], 1u);
@@ -432,7 +450,7 @@ __global__ void __launch_bounds__(256) k_rows(GraphDev g, int stage, int mode) {
       idx = idx < 0 ? 0 : (idx > g.M - 1 ? g.M - 1 : idx);
       S.bits[idx >> 5] = 0;
     }
-    for (int j = lane; j < g.G; j += 32) S.bits[g.glob[j] >> 5] = 0;
+    for (int j = lane; j < g.G; j += 32) S.bits[min(max(g.glob[j], 0), g.M - 1) >> 5] = 0;
     if (lane == 0) S.bits[0] = 0;
     __syncwarp();
   }

@@ -326,8 +326,7 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
     if (act)
       for (int tt = 0; tt < g.NT; ++tt) tids[tt * ROWS + t] = g.qids[row * g.NT + tt];
     const float thr = (pass == 1 && act) ? g.tau[row] : -INFINITY;
-    float* bs = g.bufs + row * g.capg;
-    uint16_t* bk = g.bufk + row * g.capg;
+    unsigned long long* bo = g.buf + row * g.capg;
     int cnt = 0;
     const unsigned long long* bmg = g.bmap + (int64_t)bg * g.Wpad * g.R * g.NB;
     for (int i = 0; i < ntl; ++i) {
@@ -370,6 +369,19 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
         for (int c = 0; c < 2; ++c) {
           const uint32_t cm = (uint32_t)(w[hw] >> (c * 32));
           if (!cm) continue;
+          const uint32_t kbase32 = (uint32_t)(key0 + hw * 64 + c * 32);
+          if (pass == 0) {
+            // sample pass: every candidate is kept -- predicated, no search
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if ((cm >> j) & 1u) {
+                if (cnt < g.capg)
+                  bo[cnt] = ((unsigned long long)(kbase32 + j) << 32) | __float_as_uint(sc[c * 32 + j]);
+                ++cnt;
+              }
+            }
+            continue;
+          }
           uint32_t h0 = 0, h1 = 0, h2 = 0, h3 = 0;
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
@@ -382,10 +394,8 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
           while (hit) {
             const int j = __ffs(hit) - 1;
             hit &= hit - 1;
-            if (cnt < g.capg) {
-              bs[cnt] = pick32(sc + c * 32, j);
-              bk[cnt] = (uint16_t)(key0 + hw * 64 + c * 32 + j);
-            }
+            if (cnt < g.capg)
+              bo[cnt] = ((unsigned long long)(kbase32 + j) << 32) | __float_as_uint(pick32(sc + c * 32, j));
             ++cnt;
           }
         }
@@ -439,6 +449,7 @@ static bool make_map(CUtensorMap* m, const void* base, int d, int heads, int row
 bool select_tc_supported(const GraphDev& g) {
   if (g.dtype != kDtBF16 || (g.d != 64 && g.d != 128)) return false;
   if (g.M > 65536 || g.A > 1024) return false;
+  if (g.R + 2 + (g.G < g.C ? g.G : g.C) > 32) return false;  // one special key per lane
   // TMA: 16-byte aligned strides (the base pointers are checked at launch)
   auto al = [](int64_t s) { return (s * 2) % 16 == 0; };
   if (!al(g.q_sh) || !al(g.q_sn) || !al(g.q_sb) || !al(g.k_sh) || !al(g.k_sm) || !al(g.k_sb)) return false;
