@@ -86,6 +86,17 @@ struct RowHeap {
   }
 };
 
+// Order-preserving map of a float to uint32 (ascending floats -> ascending
+// unsigned); NaN-free inputs.
+__device__ __forceinline__ uint32_t okey(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float okey_inv(uint32_t k) {
+  const uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+
 __device__ __forceinline__ bool key_member(const GraphDev& g, int bg, int r, int u, int x) {
   if (x < 0 || x >= g.M) return false;
   if (g.kcode[((int64_t)bg * g.R + r) * g.M + x] != (uint16_t)u) return false;

@@ -56,34 +56,28 @@ __global__ void __launch_bounds__(128) k_hash_queries(GraphDev g) {
 // ---------------------------------------------------------------------------
 // Warp helpers
 // ---------------------------------------------------------------------------
-// Order-preserving map of a float to uint32 (ascending floats -> ascending
-// unsigned); NaN-free inputs.
-__device__ __forceinline__ uint32_t okey(float f) {
-  const uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-__device__ __forceinline__ float okey_inv(uint32_t k) {
-  const uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
-  return __uint_as_float(u);
-}
 
-// The kth largest (1-based, kth <= n) of sc[0..n) by a 4-pass, 8-bit radix
-// select. Returns its order key T and, in *need, how many entries equal to T
-// belong to the top kth. Warp-collective.
-__device__ uint32_t warp_radix_kth(const float* sc, int n, int kth, uint32_t* hist, int* need_out) {
+// The kth largest (1-based, kth <= n) of n 16-bit keys packed four to a
+// 64-bit word (entry i in bits 16*(i%4) of word i/4), read from global memory
+// by a 2-pass, 8-bit radix select. Warp-collective.
+__device__ uint32_t warp_radix_kth16(const unsigned long long* src, int n, int kth, uint32_t* hist) {
   const int lane = threadIdx.x & 31;
+  const int nw = (n + 3) >> 2;
   uint32_t prefix = 0, pmask = 0;
   int need = kth;
-  for (int shift = 24; shift >= 0; shift -= 8) {
+  for (int shift = 8; shift >= 0; shift -= 8) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0;
     __syncwarp();
-    for (int i = lane; i < n; i += 32) {
-      const uint32_t u = okey(sc[i]);
-      if ((u & pmask) == prefix) atomicAdd(&hist[(u >> shift) & 255u], 1u);
+    for (int w = lane; w < nw; w += 32) {
+      const unsigned long long e = __ldcs(src + w);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t u = (uint32_t)(e >> (16 * q)) & 0xFFFFu;
+        if (4 * w + q < n && (u & pmask) == prefix) atomicAdd(&hist[(u >> shift) & 255u], 1u);
+      }
     }
     __syncwarp();
-    // lane L owns bins 255-8L .. 248-8L (descending)
     uint32_t c[8];
     uint32_t tot = 0;
 #pragma unroll
@@ -97,7 +91,7 @@ __device__ uint32_t warp_radix_kth(const float* sc, int n, int kth, uint32_t* hi
       const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += v;
     }
-    uint32_t before = incl - tot;  // entries in higher bins than this lane's
+    uint32_t before = incl - tot;
     int found_bin = -1;
     uint32_t found_before = 0;
 #pragma unroll
@@ -109,48 +103,179 @@ __device__ uint32_t warp_radix_kth(const float* sc, int n, int kth, uint32_t* hi
       before += c[j];
     }
     const unsigned who = __ballot_sync(0xffffffffu, found_bin >= 0);
-    const int src = __ffs(who) - 1;
-    const int bin = __shfl_sync(0xffffffffu, found_bin, src);
-    const uint32_t fb = __shfl_sync(0xffffffffu, found_before, src);
+    const int src_lane = __ffs(who) - 1;
+    const int bin = __shfl_sync(0xffffffffu, found_bin, src_lane);
+    const uint32_t fb = __shfl_sync(0xffffffffu, found_before, src_lane);
     need -= (int)fb;
     prefix |= (uint32_t)bin << shift;
     pmask |= 0xFFu << shift;
     __syncwarp();
   }
-  *need_out = need;
   return prefix;
 }
 
+// Descending bitonic sort of one value per lane.
+__device__ __forceinline__ uint32_t warp_sort_desc(uint32_t v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k2 = 2; k2 <= 32; k2 <<= 1) {
+#pragma unroll
+    for (int j2 = k2 >> 1; j2 > 0; j2 >>= 1) {
+      const uint32_t o = __shfl_xor_sync(0xffffffffu, v, j2);
+      const bool asc = (lane & k2) == 0, lower = (lane & j2) == 0;
+      v = (lower != asc) ? min(v, o) : max(v, o);
+    }
+  }
+  return v;
+}
+
+// The kth largest (1-based) order key among the participants of sc[0..n):
+// entries whose order key is >= lo (all entries if fewer than kth qualify).
+// Each round histograms the participants of the current key range [ulo, uhi]
+// into 256 bins of width 2^s (s the smallest shift that fits the range) and
+// narrows the range to the bin that holds the kth; once that bin has at most
+// 32 entries they are sorted across the warp. Returns the key T and, in
+// *need, how many entries equal to T belong to the top kth. `list` holds 32
+// entries. Warp-collective.
+__device__ uint32_t warp_select_kth(const float* sc, int n, int kth, uint32_t lo, uint32_t* hist,
+                                    uint32_t* list, int* need_out) {
+  const int lane = threadIdx.x & 31;
+  uint32_t mx = 0u, mn = 0xFFFFFFFFu, cntp = 0u;
+  for (int i = lane; i < n; i += 32) {
+    const uint32_t u = okey(sc[i]);
+    if (u >= lo) { mx = max(mx, u); mn = min(mn, u); ++cntp; }
+  }
+  if ((int)__reduce_add_sync(0xffffffffu, cntp) < kth) {
+    mx = 0u; mn = 0xFFFFFFFFu;
+    for (int i = lane; i < n; i += 32) { const uint32_t u = okey(sc[i]); mx = max(mx, u); mn = min(mn, u); }
+  }
+  uint32_t uhi = __reduce_max_sync(0xffffffffu, mx);
+  uint32_t ulo = __reduce_min_sync(0xffffffffu, mn);
+  int need = kth;
+  while (true) {
+    if (ulo == uhi) break;
+    const uint32_t span1 = uhi - ulo;  // span - 1
+    const int bl = 32 - __clz(span1);
+    const int sh = bl > 8 ? bl - 8 : 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0;
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) {
+      const uint32_t u = okey(sc[i]);
+      if (u >= ulo && u <= uhi) atomicAdd(&hist[(u - ulo) >> sh], 1u);
+    }
+    __syncwarp();
+    // lane L owns bins 255-8L .. 248-8L (descending)
+    uint32_t c[8];
+    uint32_t tot = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      c[j] = hist[255 - (lane * 8 + j)];
+      tot += c[j];
+    }
+    uint32_t incl = tot;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += v;
+    }
+    uint32_t before = incl - tot;  // entries in higher bins than this lane's
+    int found_bin = -1;
+    uint32_t found_before = 0, found_cnt = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (found_bin < 0 && before < (uint32_t)need && before + c[j] >= (uint32_t)need) {
+        found_bin = 255 - (lane * 8 + j);
+        found_before = before;
+        found_cnt = c[j];
+      }
+      before += c[j];
+    }
+    const unsigned who = __ballot_sync(0xffffffffu, found_bin >= 0);
+    const int src = __ffs(who) - 1;  // exists: the range holds at least `need` entries
+    const uint32_t bin = (uint32_t)__shfl_sync(0xffffffffu, found_bin, src);
+    need -= (int)__shfl_sync(0xffffffffu, found_before, src);
+    const uint32_t cb = __shfl_sync(0xffffffffu, found_cnt, src);
+    const uint32_t nlo = ulo + (bin << sh);
+    const uint32_t nhi = (sh == 0) ? nlo : min(uhi, nlo + ((1u << sh) - 1u));
+    ulo = nlo;
+    uhi = nhi;
+    __syncwarp();
+    if (ulo != uhi && cb <= 32u) {
+      int k = 0;
+      for (int i0 = 0; i0 < n; i0 += 32) {
+        const int i = i0 + lane;
+        uint32_t u = 0u;
+        bool m = false;
+        if (i < n) {
+          u = okey(sc[i]);
+          m = u >= ulo && u <= uhi;
+        }
+        const unsigned bm = __ballot_sync(0xffffffffu, m);
+        if (m) list[k + __popc(bm & ((1u << lane) - 1u))] = u;
+        k += __popc(bm);
+      }
+      __syncwarp();
+      const uint32_t v = warp_sort_desc((uint32_t)lane < cb ? list[lane] : 0u);
+      const uint32_t T = __shfl_sync(0xffffffffu, v, need - 1);
+      const int gt = __popc(__ballot_sync(0xffffffffu, (uint32_t)lane < cb && v > T));
+      __syncwarp();
+      *need_out = need - gt;
+      return T;
+    }
+  }
+  *need_out = need;
+  return ulo;
+}
+
 struct RowsSmem {
-  float* sc;        // [cap] scores
-  int32_t* ky;      // [cap] keys
+  float* sc;        // [max(cap, Wout)] scores; later the staged neighbor row
+  uint16_t* ky;     // [cap] keys (the tensor-core path has M <= 65536)
   uint32_t* hist;   // [256]
-  uint32_t* bits;   // [Mw] merge bitmap
-  int32_t* spec;    // [64] special keys
-  uint8_t* sflag;   // [64 * NT] replay flags
+  uint32_t* bits;   // [Mw] merge bitmap over [0, M)
+  uint32_t* l1;     // [64] nonzero words of `bits`
+  int32_t* spec;    // [64] special keys, then the ones that need a dot product
+  uint8_t* sflag;   // [32 * NT] replay flags
 };
+
+// Shared-memory bytes per warp of k_rows: THRESH needs only the histogram.
+__host__ __device__ inline size_t rows_warp_bytes(const GraphDev& g, int stage) {
+  if (stage == 0) return 256 * 4;
+  const int cap = g.capg + 64;
+  const int scn = cap > g.Wout ? cap : g.Wout;
+  const int Mw = (g.M + 31) / 32;
+  const size_t b = (size_t)scn * 4 + (((size_t)cap * 2 + 15) & ~size_t(15)) + 256 * 4 + (size_t)Mw * 4 +
+                   64 * 4 + 64 * 4 + 32 * (size_t)g.NT;
+  return (b + 15) & ~size_t(15);
+}
 
 // ---------------------------------------------------------------------------
 // k_rows
 // ---------------------------------------------------------------------------
 template <int DT, int D>
-__global__ void __launch_bounds__(256) k_rows(GraphDev g, int stage, int mode) {
+__global__ void __launch_bounds__(128, 8) k_rows(GraphDev g, int stage, int mode) {
   // stage 0 = THRESH, 1 = FINAL
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cap = g.capg + 64;
+  const int scn = cap > g.Wout ? cap : g.Wout;
   const int Mw = (g.M + 31) / 32;
-  const size_t per_warp = (size_t)cap * 8 + 256 * 4 + (size_t)Mw * 4 + 64 * 4 + 64 * (size_t)g.NT;
-  unsigned char* base = smem + warp * ((per_warp + 15) & ~size_t(15));
+  const int nl1 = (Mw + 31) / 32;
+  unsigned char* base = smem + warp * rows_warp_bytes(g, stage);
   RowsSmem S;
-  S.sc = reinterpret_cast<float*>(base);
-  S.ky = reinterpret_cast<int32_t*>(S.sc + cap);
-  S.hist = reinterpret_cast<uint32_t*>(S.ky + cap);
-  S.bits = S.hist + 256;
-  S.spec = reinterpret_cast<int32_t*>(S.bits + Mw);
-  S.sflag = reinterpret_cast<uint8_t*>(S.spec + 64);
-  if (stage == 1)
+  if (stage == 0) {
+    S.hist = reinterpret_cast<uint32_t*>(base);
+  } else {
+    S.sc = reinterpret_cast<float*>(base);
+    S.ky = reinterpret_cast<uint16_t*>(S.sc + scn);
+    S.hist = reinterpret_cast<uint32_t*>(base + (size_t)scn * 4 + (((size_t)cap * 2 + 15) & ~size_t(15)));
+    S.bits = S.hist + 256;
+    S.l1 = S.bits + Mw;
+    S.spec = reinterpret_cast<int32_t*>(S.l1 + 64);
+    S.sflag = reinterpret_cast<uint8_t*>(S.spec + 64);
     for (int i = lane; i < Mw; i += 32) S.bits[i] = 0;
+    for (int i = lane; i < 64; i += 32) S.l1[i] = 0;
+  }
   __syncwarp();
 
   const int64_t total = (int64_t)g.B * g.H * g.N;
@@ -174,13 +299,11 @@ __global__ void __launch_bounds__(256) k_rows(GraphDev g, int stage, int mode) {
         // expected at or above tau, so fewer than A (the fallback case) is
         // a 3x deviation, and more than the buffer holds (6A+64) a 2x one.
         const int x = (int)(((int64_t)3 * g.A * sampled + tiles_row - 1) / tiles_row);
-        if (x >= 1 && c >= x) {
-          for (int i = lane; i < c; i += 32) S.sc[i] = __uint_as_float((uint32_t)bo[i]);
-          __syncwarp();
-          int need;
-          const uint32_t T = warp_radix_kth(S.sc, c, x, S.hist, &need);
-          tau = okey_inv(T);
-        }
+        // The sample holds the upper 16 bits of each score's order key, so
+        // tau is rounded down to the lowest score sharing the x-th key: at
+        // least x sampled scores are >= tau.
+        const int c16 = min(cnt_all, 4 * g.capg);
+        if (x >= 1 && c16 >= x) tau = okey_inv(warp_radix_kth16(bo, c16, x, S.hist) << 16);
       }
       if (lane == 0) g.tau[row] = tau;
       __syncwarp();
@@ -195,9 +318,9 @@ __global__ void __launch_bounds__(256) k_rows(GraphDev g, int stage, int mode) {
       continue;
     }
     for (int i = lane; i < c; i += 32) {
-      const unsigned long long e = bo[i];
+      const unsigned long long e = __ldcs(bo + i);  // read once
       S.sc[i] = __uint_as_float((uint32_t)e);
-      S.ky[i] = (int32_t)(e >> 32);
+      S.ky[i] = (uint16_t)(e >> 32);
     }
     // Special keys: pad keys perm_r[M-1], causal self, empty-bucket fallbacks.
     const bool any_empty = g.qempty[row] != 0;
@@ -208,38 +331,35 @@ __global__ void __launch_bounds__(256) k_rows(GraphDev g, int stage, int mode) {
     // keeps its entry unless it is out of range or repeats an earlier one;
     // kept entries are compacted in order.
     const int ncand = g.R + 1 + (any_empty ? lim_g + 1 : 0);
-    int x = -1;
+    int xs = -1;
     if (lane < g.R) {
-      x = (int)(g.pmax[bg * g.R + lane] & 0xFFFFFu);
-      if (g.causal && x > n) x = -1;  // a future pad key never appears as itself
+      xs = (int)(g.pmax[bg * g.R + lane] & 0xFFFFFu);
+      if (g.causal && xs > n) xs = -1;  // a future pad key never appears as itself
     } else if (lane == g.R) {
-      x = g.causal ? n : -1;
+      xs = g.causal ? n : -1;
     } else if (lane < ncand - 1) {
-      x = g.glob[lane - g.R - 1];
+      xs = g.glob[lane - g.R - 1];
     } else if (lane == ncand - 1 && any_empty) {
-      x = g.G < g.C ? 0 : -1;
+      xs = g.G < g.C ? 0 : -1;
     }
-    if (x >= g.M) x = -1;
-    bool keep = x >= 0;
-    for (int z = 0; z < 32; ++z) {
-      const int y = __shfl_sync(0xffffffffu, x, z);
-      if (z < lane && y == x) keep = false;
-    }
+    if (xs >= g.M) xs = -1;
+    const unsigned same = __match_any_sync(0xffffffffu, xs);  // every lane takes part
+    const bool keep = xs >= 0 && lane == __ffs(same) - 1;
     const unsigned km = __ballot_sync(0xffffffffu, keep);
-    if (keep) S.spec[__popc(km & ((1u << lane) - 1u))] = x;
+    if (keep) S.spec[__popc(km & ((1u << lane) - 1u))] = xs;
     const int nspec = __popc(km);
     __syncwarp();
     const uint16_t* tids = g.qids + row * g.NT;
     // Replay, lane-parallel over (key, slot) pairs: flag 1 = key's slot in
     // this (round, probe) bucket is a real member, 2 = it is the overflow pad,
     // 0 = absent (or the bucket is empty: handled as a third state 3 = present
-    // via the empty-bucket fallback list).
-    for (int p = lane; p < nspec * g.NT; p += 32) {
+    // via the empty-bucket fallback list). Four pairs per lane per step, all
+    // loads issued before any is used.
+    auto replay = [&](int p) -> uint8_t {
       const int i = p / g.NT, tt = p - i * g.NT;
       const int x = S.spec[i];
       const int r = tt / (1 + g.Te);
-      const int u = tids[tt];
-      // every load issued up front (no dependent chain)
+      const int u = __ldg(tids + tt);
       const int64_t tb = (int64_t)(bg * g.R + r) * g.NB + u;
       const int sz = __ldg(g.bsize + tb);
       const int lc = __ldg(g.lastc + tb);
@@ -266,12 +386,26 @@ __global__ void __launch_bounds__(256) k_rows(GraphDev g, int stage, int mode) {
           if (P == x) f = 2;
         }
       }
-      S.sflag[p] = f;
+      return f;
+    };
+    const int npairs = nspec * g.NT;
+    for (int p0 = 0; p0 < npairs; p0 += 128) {
+      uint8_t f[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int p = p0 + j * 32 + lane;
+        f[j] = p < npairs ? replay(p) : 0;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int p = p0 + j * 32 + lane;
+        if (p < npairs) S.sflag[p] = f[j];
+      }
     }
     __syncwarp();
-    // Lane i decides special i: eligible iff its first appearance is valid.
-    int add_key = -1;
-    float add_score = 0.f;
+    // Lane i decides special i: eligible iff its first appearance is valid;
+    // an eligible key that the scan did not already keep needs its score.
+    bool need_dot = false;
     if (lane < nspec) {
       const int x = S.spec[lane];
       bool elig = false;
@@ -286,54 +420,80 @@ __global__ void __launch_bounds__(256) k_rows(GraphDev g, int stage, int mode) {
             !((__ldg(g.pmask + (int64_t)bg * g.Wpad + (x >> 6)) >> (x & 63)) & 1ull) && !(g.causal && x >= n);
         bool present = false;
         if (scanned)
-          for (int z = 0; z < c && !present; ++z) present = S.ky[z] == x;
-        if (!present) {
-          const void* qrow = row_ptr<DT>(g.q, b * g.q_sb + h * g.q_sh + (int64_t)n * g.q_sn);
+          for (int z = 0; z < c && !present; ++z) present = (int)S.ky[z] == x;
+        need_dot = !present;
+      }
+    }
+    const unsigned dm = __ballot_sync(0xffffffffu, need_dot);
+    const int ndot = __popc(dm);
+    if (need_dot) S.spec[32 + __popc(dm & ((1u << lane) - 1u))] = S.spec[lane];
+    __syncwarp();
+    // Scores of those keys: 8 lanes per key, D/8 elements per lane.
+    if (ndot > 0) {
+      constexpr int E = D / 8;
+      const int grp = lane >> 3, sub = lane & 7;
+      float qv[E];
+      const void* qrow = row_ptr<DT>(g.q, b * g.q_sb + h * g.q_sh + (int64_t)n * g.q_sn);
+#pragma unroll
+      for (int e = 0; e < E; e += 8) {
+        if (sub * E + e < g.d) {
+          load8<DT>(qrow, sub * E + e, qv + e);
+        } else {
+#pragma unroll
+          for (int z = 0; z < 8; ++z) qv[e + z] = 0.f;
+        }
+      }
+      for (int j0 = 0; j0 < ndot; j0 += 4) {
+        const int j = j0 + grp;
+        float acc = 0.f;
+        if (j < ndot) {
+          const int x = S.spec[32 + j];
           const void* krow = row_ptr<DT>(g.k, b * g.k_sb + gk * g.k_sh + (int64_t)x * g.k_sm);
-          float s0 = 0.f, s1 = 0.f;
-          for (int i = 0; i < g.d; i += 4) {
-            const float4 a = load4<DT>(qrow, i);
-            const float4 kk = load4<DT>(krow, i);
-            s0 = fmaf(a.x, kk.x, s0);
-            s1 = fmaf(a.y, kk.y, s1);
-            s0 = fmaf(a.z, kk.z, s0);
-            s1 = fmaf(a.w, kk.w, s1);
+#pragma unroll
+          for (int e = 0; e < E; e += 8) {
+            if (sub * E + e < g.d) {
+              float kv[8];
+              load8<DT>(krow, sub * E + e, kv);
+#pragma unroll
+              for (int z = 0; z < 8; ++z) acc = fmaf(qv[e + z], kv[z], acc);
+            }
           }
-          add_key = x;
-          add_score = s0 + s1;
+        }
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+        if (j < ndot && sub == 0) {
+          S.sc[c + j] = acc;
+          S.ky[c + j] = (uint16_t)S.spec[32 + j];
         }
       }
     }
-    const unsigned am = __ballot_sync(0xffffffffu, add_key >= 0);
-    if (add_key >= 0) {
-      const int pos = c + __popc(am & ((1u << lane) - 1u));
-      S.sc[pos] = add_score;
-      S.ky[pos] = add_key;
-    }
-    const int tot = c + __popc(am);
+    const int tot = c + ndot;
     __syncwarp();
 
-    // Exact top-A (the whole pool when it has at most A entries).
+    // Exact top-A (the whole pool when it has at most A entries). At least A
+    // entries reached tau, so the A-th largest is >= tau and only those take
+    // part in the select.
     const int n_elig = min(tot, g.A);
-    uint32_t T = 0;
-    int need = 0;
-    if (tot > g.A) T = warp_radix_kth(S.sc, tot, g.A, S.hist, &need);
-    // Compact the selection to the front: keys > T, then `need` keys == T in
-    // index order (ties are the reference's unspecified topk order).
     if (tot > g.A) {
+      const float tz = tau == 0.f ? -0.f : tau;
+      const uint32_t lo = tau > -INFINITY ? okey(tz) : 0u;
+      int need;
+      const uint32_t T = warp_select_kth(S.sc, tot, g.A, lo, S.hist, reinterpret_cast<uint32_t*>(S.spec), &need);
+      // Compact the selection to the front: keys > T, then `need` keys == T
+      // in index order (ties are the reference's unspecified topk order).
       int wpos = 0, eq_seen = 0;
-      // two sweeps keep the write position <= read position
       for (int i0 = 0; i0 < tot; i0 += 32) {
         const int i = i0 + lane;
         const bool in = i < tot;
-        const uint32_t u = in ? okey(S.sc[i]) : 0u;
+        const float sv = in ? S.sc[i] : 0.f;
+        const uint16_t kv = in ? S.ky[i] : 0;
+        const uint32_t u = okey(sv);
         const bool eq = in && u == T;
         const unsigned eqm = __ballot_sync(0xffffffffu, eq);
         const int eq_rank = eq_seen + __popc(eqm & ((1u << lane) - 1u));
         const bool sel = in && (u > T || (eq && eq_rank < need));
         const unsigned sm = __ballot_sync(0xffffffffu, sel);
-        const float sv = in ? S.sc[i] : 0.f;
-        const int kv = in ? S.ky[i] : 0;
         __syncwarp();
         if (sel) {
           const int dst = wpos + __popc(sm & ((1u << lane) - 1u));
@@ -354,7 +514,7 @@ __global__ void __launch_bounds__(256) k_rows(GraphDev g, int stage, int mode) {
       while (P2 < n_elig) P2 <<= 1;
       for (int i = n_elig + lane; i < P2; i += 32) {
         S.sc[i] = -INFINITY;
-        S.ky[i] = 0x7fffffff;
+        S.ky[i] = 0xFFFF;
       }
       __syncwarp();
       for (int k2 = 2; k2 <= P2; k2 <<= 1) {
@@ -367,7 +527,7 @@ __global__ void __launch_bounds__(256) k_rows(GraphDev g, int stage, int mode) {
               if ((a < bb) == desc) {
                 S.sc[i] = bb;
                 S.sc[ixj] = a;
-                const int t0 = S.ky[i];
+                const uint16_t t0 = S.ky[i];
                 S.ky[i] = S.ky[ixj];
                 S.ky[ixj] = t0;
               }
@@ -377,81 +537,112 @@ __global__ void __launch_bounds__(256) k_rows(GraphDev g, int stage, int mode) {
         }
       }
       int32_t* out = g.lsh + row * g.A;
-      for (int j = lane; j < g.A; j += 32) out[j] = j < n_elig ? S.ky[j] : (j < g.G ? g.glob[j] : 0);
+      for (int j = lane; j < g.A; j += 32) out[j] = j < n_elig ? (int)S.ky[j] : (j < g.G ? g.glob[j] : 0);
       __syncwarp();
       continue;
     }
     if (g.lsh) {
       int32_t* out = g.lsh + row * g.A;
-      for (int j = lane; j < g.A; j += 32) out[j] = j < n_elig ? S.ky[j] : (j < g.G ? g.glob[j] : 0);
+      for (int j = lane; j < g.A; j += 32) out[j] = j < n_elig ? (int)S.ky[j] : (j < g.G ? g.glob[j] : 0);
     }
-    // Merge through a bitmap over [0, M): LSH keys, window, globals, key 0
-    // from the fallback slots; self excluded, then emitted in ascending order.
+    // ---- merge: self, then the ascending union of window, globals, LSH keys
+    // and key 0 from the fallback slots, self excluded. The window is a
+    // contiguous key range [wlo, whi] (indices clamped to [0, M), causal
+    // offsets > 0 mapped to self), so only the other keys go through a
+    // bitmap; the window's keys then take consecutive slots after the
+    // bitmap keys below wlo.
     const bool add_zero = max(n_elig, g.G) < g.A;
-    const int kw = g.is_cross ? 0 : 2 * g.window + 1;
-    for (int j = lane; j < n_elig; j += 32) {
-      const int x = S.ky[j];
-      atomicOr(&S.bits[x >> 5], 1u << (x & 31));
+    const bool drop_self = !g.is_cross && n < g.M;
+    int wlo = 1, whi = 0, nwin = 0;
+    if (!g.is_cross) {
+      wlo = min(max(n - g.window, 0), g.M - 1);
+      whi = min(max(g.causal ? n : n + g.window, 0), g.M - 1);
+      nwin = whi - wlo + 1 - ((drop_self && n >= wlo && n <= whi) ? 1 : 0);
     }
-    for (int j = lane; j < kw; j += 32) {
-      const int o = j - g.window;
-      int idx = (g.causal && o > 0) ? n : n + o;
-      idx = idx < 0 ? 0 : (idx > g.M - 1 ? g.M - 1 : idx);
-      atomicOr(&S.bits[idx >> 5], 1u << (idx & 31));
-    }
-    for (int j = lane; j < g.G; j += 32) {
-      const int x = min(max(g.glob[j], 0), g.M - 1);
-      atomicOr(&S.bits[x >> 5], 1u << (x & 31));
-    }
-    if (add_zero && lane == 0) atomicOr(&S.bits[0], 1u);
+    auto mark = [&](int x) {
+      if (x >= wlo && x <= whi) return;  // window key (or self inside it)
+      if (drop_self && x == n) return;
+      const uint32_t old = atomicOr(&S.bits[x >> 5], 1u << (x & 31));
+      if (old == 0u) atomicOr(&S.l1[x >> 10], 1u << ((x >> 5) & 31));
+    };
+    for (int j = lane; j < n_elig; j += 32) mark(S.ky[j]);
+    for (int j = lane; j < g.G; j += 32) mark(min(max(g.glob[j], 0), g.M - 1));
+    if (add_zero && lane == 0) mark(0);
     __syncwarp();
-    if (!g.is_cross && lane == 0 && n < g.M) atomicAnd(&S.bits[n >> 5], ~(1u << (n & 31)));
-    __syncwarp();
-    int32_t* nbo = g.nb + row * g.Wout;
-    uint8_t* vo = g.valid + row * g.Wout;
-    const int s0 = g.is_cross ? 0 : 1;
-    if (!g.is_cross && lane == 0) {
-      nbo[0] = min(n, g.M - 1);
-      vo[0] = 1;
-    }
-    // Lane L scans words [L*wpl, (L+1)*wpl); exclusive scan of popcounts.
+    // Lane L owns bitmap words [L*wpl, (L+1)*wpl) and visits the nonzero
+    // ones through the summary words: count its keys (and those below wlo),
+    // exclusive-scan across lanes, then emit.
     const int wpl = (Mw + 31) / 32;
-    const int w0 = lane * wpl, w1 = min(Mw, w0 + wpl);
-    int my = 0;
-    for (int wd = w0; wd < w1; ++wd) my += __popc(S.bits[wd]);
-    int incl = my;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    int slot = s0 + incl - my;
-    for (int wd = w0; wd < w1 && slot < g.Wout; ++wd) {
-      uint32_t bw = S.bits[wd];
-      while (bw && slot < g.Wout) {
-        const int bit = __ffs(bw) - 1;
-        bw &= bw - 1u;
-        nbo[slot] = wd * 32 + bit;
-        vo[slot] = 1;
-        ++slot;
+    const int w0 = min(lane * wpl, Mw), w1 = min(w0 + wpl, Mw);
+    auto lane_words = [&](int l) -> uint32_t {
+      uint32_t m1 = S.l1[l];
+      const int lb = l * 32;
+      if (w0 > lb) m1 &= ~((1u << (w0 - lb)) - 1u);
+      if (w1 < lb + 32) m1 &= (1u << (w1 - lb)) - 1u;
+      return m1;
+    };
+    int cnt = 0, below = 0;
+    if (w0 < w1) {
+      for (int l = w0 >> 5; l <= (w1 - 1) >> 5; ++l) {
+        uint32_t m1 = lane_words(l);
+        while (m1) {
+          const int wd = l * 32 + __ffs(m1) - 1;
+          m1 &= m1 - 1u;
+          const uint32_t bw = S.bits[wd];
+          cnt += __popc(bw);
+          const int lo_rel = wlo - wd * 32;  // keys below wlo in this word
+          if (lo_rel >= 32) below += __popc(bw);
+          else if (lo_rel > 0) below += __popc(bw & ((1u << lo_rel) - 1u));
+        }
       }
     }
-    const int total_set = __shfl_sync(0xffffffffu, incl, 31);
-    for (int j = s0 + total_set + lane; j < g.Wout; j += 32) {
-      nbo[j] = 0;
-      vo[j] = 0;
+    int incl = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += v;
+    }
+    const int nlg = __shfl_sync(0xffffffffu, incl, 31);
+    const int nbelow = __reduce_add_sync(0xffffffffu, below);
+    const int s0 = g.is_cross ? 0 : 1;
+    int* stage_out = reinterpret_cast<int*>(S.sc);  // the scores are no longer needed
+    __syncwarp();
+    if (w0 < w1) {
+      int rank = incl - cnt;
+      for (int l = w0 >> 5; l <= (w1 - 1) >> 5; ++l) {
+        uint32_t m1 = lane_words(l);
+        while (m1) {
+          const int wd = l * 32 + __ffs(m1) - 1;
+          m1 &= m1 - 1u;
+          uint32_t bw = S.bits[wd];
+          S.bits[wd] = 0u;
+          while (bw) {
+            const int x = wd * 32 + __ffs(bw) - 1;
+            bw &= bw - 1u;
+            const int slot = s0 + rank + (x > whi ? nwin : 0);
+            if (slot < g.Wout) stage_out[slot] = x;
+            ++rank;
+          }
+        }
+      }
     }
     __syncwarp();
-    // clear the bitmap words this row touched
-    for (int j = lane; j < n_elig; j += 32) S.bits[S.ky[j] >> 5] = 0;
-    for (int j = lane; j < kw; j += 32) {
-      const int o = j - g.window;
-      int idx = (g.causal && o > 0) ? n : n + o;
-      idx = idx < 0 ? 0 : (idx > g.M - 1 ? g.M - 1 : idx);
-      S.bits[idx >> 5] = 0;
+    for (int j = lane; j < nwin; j += 32) {
+      int x = wlo + j;
+      if (drop_self && x >= n) ++x;  // skip self
+      const int slot = s0 + nbelow + j;
+      if (slot < g.Wout) stage_out[slot] = x;
     }
-    for (int j = lane; j < g.G; j += 32) S.bits[min(max(g.glob[j], 0), g.M - 1) >> 5] = 0;
-    if (lane == 0) S.bits[0] = 0;
+    if (s0 == 1 && lane == 0) stage_out[0] = min(n, g.M - 1);
+    __syncwarp();
+    const int total = min(s0 + nlg + nwin, g.Wout);
+    int32_t* nbo = g.nb + row * g.Wout;
+    uint8_t* vo = g.valid + row * g.Wout;
+    for (int j = lane; j < g.Wout; j += 32) {
+      nbo[j] = j < total ? stage_out[j] : 0;
+      vo[j] = j < total ? 1 : 0;
+    }
+    for (int l = lane; l < nl1; l += 32) S.l1[l] = 0u;
     __syncwarp();
   }
 }
@@ -481,26 +672,27 @@ cudaError_t launch_hash_queries(const GraphDev& g, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-size_t rows_smem_bytes(const GraphDev& g, int warps) {
-  const int cap = g.capg + 64;
-  const int Mw = (g.M + 31) / 32;
-  const size_t per_warp = (size_t)cap * 8 + 256 * 4 + (size_t)Mw * 4 + 64 * 4 + 64 * (size_t)g.NT;
-  return (size_t)warps * ((per_warp + 15) & ~size_t(15));
-}
+size_t rows_smem_bytes(const GraphDev& g, int warps) { return (size_t)warps * rows_warp_bytes(g, 1); }
 
 cudaError_t launch_rows(const GraphDev& g, int stage, int mode, cudaStream_t st) {
-  int warps = 8;
-  while (warps > 1 && rows_smem_bytes(g, warps) > 200 * 1024) warps >>= 1;
-  const size_t sm = rows_smem_bytes(g, warps);
+  constexpr int kWarps = 4;
+  const size_t sm = (size_t)kWarps * rows_warp_bytes(g, stage);
   if (sm > 227 * 1024) return cudaErrorInvalidConfiguration;
-  const int64_t rows = (int64_t)g.B * g.H * g.N;
-  int64_t blocks = (rows + warps - 1) / warps;
-  if (blocks > 148 * 64) blocks = 148 * 64;
-  cudaError_t e;
   auto fn = g.dtype == kDtF32 ? (g.d <= 64 ? k_rows<kDtF32, 64> : k_rows<kDtF32, 128>)
                               : (g.d <= 64 ? k_rows<kDtBF16, 64> : k_rows<kDtBF16, 128>);
+  cudaError_t e;
   if ((e = smem_attr(fn, sm)) != cudaSuccess) return e;
-  fn<<<(unsigned)blocks, warps * 32, sm, st>>>(g, stage, mode);
+  int per_sm = 0;
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kWarps * 32, sm)) != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  int dev = 0, nsm = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+  const int64_t rows = (int64_t)g.B * g.H * g.N;
+  int64_t blocks = (rows + kWarps - 1) / kWarps;
+  const int64_t resident = (int64_t)nsm * per_sm;
+  if (blocks > resident) blocks = resident;
+  fn<<<(unsigned)blocks, kWarps * 32, sm, st>>>(g, stage, mode);
   return cudaGetLastError();
 }
 

@@ -328,6 +328,7 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
     const float thr = (pass == 1 && act) ? g.tau[row] : -INFINITY;
     unsigned long long* bo = g.buf + row * g.capg;
     int cnt = 0;
+    unsigned long long pack = 0ull;  // sample pass: up to 3 pending entries
     const unsigned long long* bmg = g.bmap + (int64_t)bg * g.Wpad * g.R * g.NB;
     for (int i = 0; i < ntl; ++i) {
       const int sb = i & 1;
@@ -371,13 +372,17 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
           if (!cm) continue;
           const uint32_t kbase32 = (uint32_t)(key0 + hw * 64 + c * 32);
           if (pass == 0) {
-            // sample pass: every candidate is kept -- predicated, no search
+            // Sample pass: every candidate's 16-bit order-key prefix, packed
+            // four to a 64-bit store (the threshold needs no keys).
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               if ((cm >> j) & 1u) {
-                if (cnt < g.capg)
-                  bo[cnt] = ((unsigned long long)(kbase32 + j) << 32) | __float_as_uint(sc[c * 32 + j]);
+                pack |= (unsigned long long)(okey(sc[c * 32 + j]) >> 16) << (16 * (cnt & 3));
                 ++cnt;
+                if ((cnt & 3) == 0) {
+                  if (cnt <= 4 * g.capg) bo[(cnt >> 2) - 1] = pack;
+                  pack = 0ull;
+                }
               }
             }
             continue;
@@ -401,7 +406,10 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
         }
       }
     }
-    if (act) g.rcnt[row] = cnt;
+    if (act) {
+      if (pass == 0 && (cnt & 3) && cnt <= 4 * g.capg) bo[cnt >> 2] = pack;
+      g.rcnt[row] = cnt;
+    }
   }
   tc_fence_before();
   __syncthreads();
