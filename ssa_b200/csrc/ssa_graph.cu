@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(256) k_hash_keys(GraphDev g) {
     const unsigned peers = __match_any_sync(amask, code);
     if (lane == __ffs(peers) - 1) {
       const unsigned long long bits = (unsigned long long)peers << (wbase & 63);
-      atomicOr(&g.bmap[(((int64_t)bg * g.Wpad + (wbase >> 6)) * g.R + r) * g.NB + code], bits);
+      atomicOr(&g.bmap[bmap_idx(g, bg, wbase >> 6, r, (int)code)], bits);
     }
     // perm[M-1] of the stable sort = largest key of the highest bucket.
     const uint32_t packed = (code << 20) | (uint32_t)m;
@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(256) k_bucket_trim(GraphDev g) {
   for (int u = threadIdx.x; u < g.NB; u += blockDim.x) {
     int run = 0, last = -1;
     for (int w = 0; w < g.W; ++w) {
-      unsigned long long* ptr = &g.bmap[(((int64_t)bg * g.Wpad + w) * g.R + r) * g.NB + u];
+      unsigned long long* ptr = &g.bmap[bmap_idx(g, bg, w, r, u)];
       unsigned long long x = *ptr;
       if (!x) continue;
       const int c = __popcll(x);
@@ -205,11 +205,10 @@ __global__ void k_select_merge(GraphDev g, int mode) {
     }
     __syncthreads();
     if (!act) continue;
-    const unsigned long long* bm = g.bmap + ((int64_t)bg * g.Wpad + kt) * g.R * g.NB;
     unsigned long long w = 0ull;
     for (int tt = 0; tt < g.NT; ++tt) {
       const int r = tt / (1 + g.Te);
-      w |= __ldg(bm + r * g.NB + tids[tt * rows + t]);
+      w |= __ldg(&g.bmap[bmap_idx(g, bg, kt, r, tids[tt * rows + t])]);
     }
     w &= ~__ldg(g.pmask + (int64_t)bg * g.Wpad + kt);
     if (g.causal) {  // keys < n only; n itself is a special key

@@ -23,7 +23,7 @@ struct GraphDev {
   void* ws;
   size_t zero_off, zero_bytes;
   uint16_t* kcode;                // [BG][R][M] bucket id of every key
-  unsigned long long* bmap;       // [BG][W][R][NB] first-C member masks
+  unsigned long long* bmap;       // [BG][Wpad/2][R][NB][2] first-C member masks (bmap_idx)
   unsigned long long* pmask;      // [BG][W] pad keys perm_r[M-1]
   uint32_t* pmax;                 // [BG][R] (bucket << 20 | key) of perm_r[M-1]
   int32_t* bsize;                 // [BG][R][NB]
@@ -41,6 +41,13 @@ struct GraphDev {
   int32_t* nb;                    // [B][H][N][Wout]
   uint8_t* valid;                 // [B][H][N][Wout]
 };
+
+// Index of the member mask of 64-key word w, round r, bucket u. The two words
+// of a 128-key tile are adjacent, so one tile's masks for all (round, bucket)
+// pairs form one contiguous block of R * NB * 16 bytes.
+__host__ __device__ inline int64_t bmap_idx(const GraphDev& g, int bg, int w, int r, int u) {
+  return ((((int64_t)bg * (g.Wpad >> 1) + (w >> 1)) * g.R + r) * g.NB + u) * 2 + (w & 1);
+}
 
 // Fills the workspace pointers of g (g->ws may be null to only size it) and
 // returns the bytes needed. Decides g->use_tc from the shapes.

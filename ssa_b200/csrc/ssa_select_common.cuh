@@ -101,7 +101,7 @@ __device__ __forceinline__ bool key_member(const GraphDev& g, int bg, int r, int
   if (x < 0 || x >= g.M) return false;
   if (g.kcode[((int64_t)bg * g.R + r) * g.M + x] != (uint16_t)u) return false;
   const unsigned long long w =
-      __ldg(&g.bmap[(((int64_t)bg * g.Wpad + (x >> 6)) * g.R + r) * g.NB + u]);
+      __ldg(&g.bmap[bmap_idx(g, bg, x >> 6, r, u)]);
   return (w >> (x & 63)) & 1ull;
 }
 

@@ -366,7 +366,7 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g, int stage, int mode
       const uint32_t pm = __ldg(g.pmax + bg * g.R + r);
       const uint16_t code = __ldg(g.kcode + ((int64_t)bg * g.R + r) * g.M + x);
       const unsigned long long wbits =
-          __ldg(&g.bmap[(((int64_t)bg * g.Wpad + (x >> 6)) * g.R + r) * g.NB + u]);
+          __ldg(&g.bmap[bmap_idx(g, bg, x >> 6, r, u)]);
       const bool member = code == (uint16_t)u && ((wbits >> (x & 63)) & 1ull);
       uint8_t f = 0;
       if (sz == 0) {

@@ -1,19 +1,23 @@
 // ssa_select_tc.cu -- tensor-core (tcgen05) candidate scan for bf16 inputs.
 //
-// Same selection as k_select_merge (ssa_graph.cu), but the q.k scores come
-// from 5th-generation tensor cores instead of per-candidate FMA loops:
+// Computes the same candidate scores as k_select_merge (ssa_graph.cu), with
+// 5th-generation tensor cores instead of per-candidate FMA loops. One CTA
+// per 128-row query tile:
 //
-//   warp 4 (one lane)  TMA: the CTA's 128-row q tile once, then 128-key tiles
-//                      of K into a 2-stage ring (SWIZZLE_128B, K-major).
+//   warp 4 (one lane)  TMA: the q tile once, then 128-key tiles of K into a
+//                      ring of up to 4 stages (SWIZZLE_128B, K-major), and a
+//                      bulk copy of each key tile's member-mask block (all
+//                      rounds and buckets, R * NB * 16 bytes) into a second
+//                      ring when that block is at most 8 KB.
 //   warp 5             allocates 256 TMEM columns; one lane issues
 //                      tcgen05.mma (M=128, N=128, K=16, bf16 in, fp32 out)
 //                      for S = Q K^T into one of two TMEM accumulators, and
 //                      tcgen05.commit releases the K stage and publishes S.
-//   warps 0-3          thread per query row (TMEM lane = row): tcgen05.ld the
-//                      row's 128 scores, OR the row's bucket masks for the
-//                      tile, and push candidates that beat the heap minimum
-//                      into the row's shared-memory top-A heap; then the
-//                      special-key replay and the merge, as in ssa_graph.cu.
+//   warps 0-3          thread per query row (TMEM lane = row): OR the row's
+//                      bucket masks for the tile, tcgen05.ld the row's 128
+//                      scores, and append the candidates to the row's global
+//                      buffer -- all of them in the sample pass (16-bit order
+//                      keys), those with score >= tau in the full pass.
 //
 // bf16 x bf16 products are exact in fp32, so tensor-core scores differ from
 // the reference's fp32 sums only by accumulation order (rescore ties).
@@ -105,6 +109,16 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Plain bulk copy global -> shared (16-byte aligned addresses, size a
+// multiple of 16), completing on the mbarrier's transaction count.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // K-major, SWIZZLE_128B operand descriptor (canonical layout: 8-row groups of
 // 128-byte rows, 1024 bytes apart; LBO unused for this layout = 1).
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
@@ -175,11 +189,18 @@ __device__ __forceinline__ float pick32(const float* a, int j) {
 }
 
 struct SmemPlan {
-  uint32_t q, k, tids, bars, tmem_slot, total;
-  int stages;
+  uint32_t q, k, bm, toff, bars, tmem_slot, total;
+  int stages, bstages;
+  uint32_t bm_bytes;
 };
 
-__host__ __device__ inline SmemPlan plan_stages(int D, int NT, int stages) {
+// Bytes of one key tile's member masks for all (round, bucket) pairs; the
+// scan stages them in shared memory when they are at most 8 KB.
+__host__ __device__ inline uint32_t bm_tile_bytes(const GraphDev& g) {
+  return (uint32_t)g.R * (uint32_t)g.NB * 16u;
+}
+
+__host__ __device__ inline SmemPlan plan_stages(int D, int NT, int stages, uint32_t bm_bytes, int bstages) {
   SmemPlan p;
   uint32_t off = 0;
   auto take = [&](uint32_t bytes, uint32_t align) {
@@ -191,8 +212,9 @@ __host__ __device__ inline SmemPlan plan_stages(int D, int NT, int stages) {
   const uint32_t atoms = (uint32_t)D / 64;
   p.q = take(atoms * ROWS * 128, 1024);
   p.k = take((uint32_t)stages * atoms * NKEY * 128, 1024);
-  p.tids = take((uint32_t)NT * ROWS * 2, 16);
-  p.bars = take(16 * 8, 8);
+  p.bm = take((uint32_t)bstages * bm_bytes, 128);
+  p.toff = take((uint32_t)NT * ROWS * 2, 16);
+  p.bars = take(24 * 8, 8);
   p.tmem_slot = take(16, 16);
   // At least 80 KB per CTA so that at most two CTAs share an SM: two CTAs
   // use all 512 TMEM columns, a third would wait in tcgen05.alloc.
@@ -200,16 +222,22 @@ __host__ __device__ inline SmemPlan plan_stages(int D, int NT, int stages) {
   if (total < 80 * 1024) total = 80 * 1024;
   p.total = total;
   p.stages = stages;
+  p.bstages = bstages;
+  p.bm_bytes = bstages ? bm_bytes : 0u;
   return p;
 }
 
-// The deepest K ring (up to 4 stages) that keeps two CTAs per SM.
-__host__ __device__ inline SmemPlan plan(int D, int NT) {
-  for (int st = 4; st > 2; --st) {
-    const SmemPlan p = plan_stages(D, NT, st);
-    if (p.total <= 113 * 1024) return p;
-  }
-  return plan_stages(D, NT, 2);
+// The deepest K ring (up to 4 stages) that keeps two CTAs per SM, with a
+// 3-stage (else 2-stage) ring of mask blocks when those are staged.
+__host__ __device__ inline SmemPlan plan(int D, const GraphDev& g) {
+  const uint32_t bmb = bm_tile_bytes(g);
+  const bool staged = bmb <= 8192u;
+  for (int bst = staged ? 3 : 0; bst >= (staged ? 2 : 0); --bst)
+    for (int st = 4; st >= 2; --st) {
+      const SmemPlan p = plan_stages(D, g.NT, st, bmb, bst);
+      if (p.total <= 113 * 1024) return p;
+    }
+  return plan_stages(D, g.NT, 2, bmb, 0);
 }
 
 }  // namespace tc
@@ -228,11 +256,14 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int ATOMS = D / 64;
-  const SmemPlan sp = plan(D, g.NT);
+  const SmemPlan sp = plan(D, g);
   const int NS = sp.stages;
+  const int NB_ST = sp.bstages;     // 0: masks read from global memory
+  const uint32_t bmb = sp.bm_bytes;
   unsigned char* qs = smem + sp.q;
   unsigned char* ks = smem + sp.k;
-  uint16_t* tids = reinterpret_cast<uint16_t*>(smem + sp.tids);
+  unsigned char* bms = smem + sp.bm;
+  uint16_t* toff = reinterpret_cast<uint16_t*>(smem + sp.toff);  // [NT][ROWS] r * NB + bucket
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + sp.bars);
   uint64_t* kfull = bars;           // [NS] K stage loaded (TMA tx)
   uint64_t* kempty = bars + 4;      // [NS] K stage consumed (MMA commit)
@@ -240,6 +271,8 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
   uint64_t* sempty = bars + 10;     // [2] S accumulator drained (4 epilogue warps)
   uint64_t* qfull = bars + 12;      // q tile loaded
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 13);
+  uint64_t* bfull = bars + 14;      // [NB_ST] mask block loaded (bulk tx)
+  uint64_t* bempty = bars + 18;     // [NB_ST] mask block read (4 epilogue warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + sp.tmem_slot);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -262,6 +295,10 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
       mbar_init(sfull + i, 1);
       mbar_init(sempty + i, 4);
     }
+    for (int i = 0; i < NB_ST; ++i) {
+      mbar_init(bfull + i, 1);
+      mbar_init(bempty + i, 4);
+    }
     mbar_init(qfull, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -283,7 +320,8 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
       mbar_expect_tx(qfull, ATOMS * ROWS * 128);
       for (int a = 0; a < ATOMS; ++a)
         tma_load_4d(qs + a * ROWS * 128, &qmap, qfull, a * 64, h, n0, b);
-      int issued = 0;
+      int issued = 0, issued_b = 0;
+      const unsigned long long* bmg = g.bmap + bmap_idx(g, bg, 0, 0, 0);
       for (int i = 0; i < ntl; ++i) {
         const int s = i % NS;
         if (!mbar_wait(kempty + s, ((i / NS) & 1) ^ 1, abort_flag, 11)) break;
@@ -291,10 +329,18 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
         for (int a = 0; a < ATOMS; ++a)
           tma_load_4d(ks + (s * ATOMS + a) * NKEY * 128, &kmap, kfull + s, a * 64, gk, i * step * NKEY, b);
         issued = i + 1;
+        if (NB_ST) {
+          const int sb2 = i % NB_ST;
+          if (!mbar_wait(bempty + sb2, ((i / NB_ST) & 1) ^ 1, abort_flag, 18)) break;
+          mbar_expect_tx(bfull + sb2, bmb);
+          bulk_load(bms + sb2 * bmb, bmg + (int64_t)(i * step) * g.R * g.NB * 2, bmb, bfull + sb2);
+          issued_b = i + 1;
+        }
       }
       // Do not leave while copies are in flight.
       mbar_drain(qfull, 0);
       for (int i = max(0, issued - NS); i < issued; ++i) mbar_drain(kfull + i % NS, (i / NS) & 1);
+      for (int i = max(0, issued_b - NB_ST); i < issued_b; ++i) mbar_drain(bfull + i % NB_ST, (i / NB_ST) & 1);
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
@@ -324,25 +370,44 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
     const bool act = n < g.N;
     const int64_t row = (int64_t)bh * g.N + n;
     if (act)
-      for (int tt = 0; tt < g.NT; ++tt) tids[tt * ROWS + t] = g.qids[row * g.NT + tt];
+      for (int tt = 0; tt < g.NT; ++tt)
+        toff[tt * ROWS + t] = (uint16_t)((tt / (1 + g.Te)) * g.NB + g.qids[row * g.NT + tt]);
     const float thr = (pass == 1 && act) ? g.tau[row] : -INFINITY;
     unsigned long long* bo = g.buf + row * g.capg;
     int cnt = 0;
     unsigned long long pack = 0ull;  // sample pass: up to 3 pending entries
-    const unsigned long long* bmg = g.bmap + (int64_t)bg * g.Wpad * g.R * g.NB;
+    const uint4* bmg4 = reinterpret_cast<const uint4*>(g.bmap + bmap_idx(g, bg, 0, 0, 0));
     for (int i = 0; i < ntl; ++i) {
       const int sb = i & 1;
       const int kt = i * step;
       const int key0 = kt * NKEY;
-      // Candidate masks first: their loads overlap the wait for S.
+      // Candidate masks first: they overlap the wait for S. Each (round,
+      // bucket) entry holds the tile's two 64-key words.
       unsigned long long w[2] = {0ull, 0ull};
+      if (NB_ST) {
+        const int sb2 = i % NB_ST;
+        if (!mbar_wait_warp(bfull + sb2, (i / NB_ST) & 1, abort_flag, 19)) break;
+        const uint4* bt = reinterpret_cast<const uint4*>(bms + sb2 * bmb);
+        if (act)
+          for (int tt = 0; tt < g.NT; ++tt) {
+            const uint4 v = bt[toff[tt * ROWS + t]];
+            w[0] |= ((unsigned long long)v.y << 32) | v.x;
+            w[1] |= ((unsigned long long)v.w << 32) | v.z;
+          }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bempty + sb2);
+      } else if (act) {
+        const uint4* bt = bmg4 + (int64_t)kt * g.R * g.NB;
+        for (int tt = 0; tt < g.NT; ++tt) {
+          const uint4 v = __ldg(bt + toff[tt * ROWS + t]);
+          w[0] |= ((unsigned long long)v.y << 32) | v.x;
+          w[1] |= ((unsigned long long)v.w << 32) | v.z;
+        }
+      }
       if (act) {
 #pragma unroll
         for (int hw = 0; hw < 2; ++hw) {
-          const unsigned long long* bm = bmg + (int64_t)(2 * kt + hw) * g.R * g.NB;
-          unsigned long long x = 0ull;
-          for (int tt = 0; tt < g.NT; ++tt)
-            x |= __ldg(bm + (tt / (1 + g.Te)) * g.NB + tids[tt * ROWS + t]);
+          unsigned long long x = w[hw];
           x &= ~__ldg(g.pmask + (int64_t)bg * g.Wpad + 2 * kt + hw);
           if (g.causal) {
             const int lim = n - (key0 + 64 * hw);
@@ -461,7 +526,8 @@ bool select_tc_supported(const GraphDev& g) {
   // TMA: 16-byte aligned strides (the base pointers are checked at launch)
   auto al = [](int64_t s) { return (s * 2) % 16 == 0; };
   if (!al(g.q_sh) || !al(g.q_sn) || !al(g.q_sb) || !al(g.k_sh) || !al(g.k_sm) || !al(g.k_sb)) return false;
-  const tc::SmemPlan sp = tc::plan(g.d, g.NT);
+  if ((int64_t)g.R * g.NB > 65535) return false;  // 16-bit mask-block offsets
+  const tc::SmemPlan sp = tc::plan(g.d, g);
   if (sp.total > 113 * 1024) return false;
   if (rows_smem_bytes(g, 1) > 227 * 1024) return false;
   return encode_fn() != nullptr;
@@ -474,7 +540,7 @@ bool select_tc_pointers_ok(const GraphDev& g) {
 template <int D>
 static cudaError_t launch_scan_t(const GraphDev& g, int pass, const CUtensorMap& qmap,
                                  const CUtensorMap& kmap, cudaStream_t st) {
-  const tc::SmemPlan sp = tc::plan(D, g.NT);
+  const tc::SmemPlan sp = tc::plan(D, g);
   auto fn = k_scan_tc<D>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp.total);
   if (e != cudaSuccess) return e;
