@@ -367,7 +367,15 @@ size_t graph_workspace_layout(GraphDev* g) {
   const int64_t NB = int64_t(1) << g->p;
   const int64_t rows = (int64_t)g->B * g->H * g->N;
   g->capg = ((6 * g->A + 64) + 7) / 8 * 8;
-  g->sample_s = g->A / 12 > 1 ? g->A / 12 : 1;
+  // Every s-th key tile is sampled (about 12 / A of them); the sampled
+  // tiles' records must fit the row buffer.
+  {
+    const int tiles = (g->M + 127) / 128;
+    const int fit = (int)((size_t)g->capg * 8 / kSampleTileBytes);
+    int s = g->A / 12 > 1 ? g->A / 12 : 1;
+    if (fit > 0 && (tiles + s - 1) / s > fit) s = (tiles + fit - 1) / fit;
+    g->sample_s = s;
+  }
   g->use_tc = select_tc_supported(*g) ? 1 : 0;
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -390,7 +398,7 @@ size_t graph_workspace_layout(GraphDev* g) {
     o_qids = take(sizeof(uint16_t) * rows * g->NT);
     o_qempty = take(rows);
     o_tau = take(sizeof(float) * rows);
-    o_rcnt = take(sizeof(int32_t) * rows);
+    o_rcnt = take(sizeof(int32_t) * rows * 2);
     o_buf = take(sizeof(unsigned long long) * rows * g->capg);
   }
   if (g->ws) {

@@ -33,14 +33,19 @@ struct GraphDev {
   uint16_t* qids;                 // [B*H*N][NT] bucket id per (round, probe) slot
   uint8_t* qempty;                // [B*H*N] some slot's bucket is empty
   float* tau;                     // [B*H*N] scan threshold
-  int32_t* rcnt;                  // [B*H*N] kept candidates (> capg: overflow)
-  unsigned long long* buf;        // [B*H*N][capg] kept (key << 32 | score bits)
+  int32_t* rcnt;                  // [B*H*N][2] kept candidates per scan group (> capg/2: overflow)
+  unsigned long long* buf;        // [B*H*N][capg] kept (key << 32 | score bits); in the
+                                  // sample pass kSampleTileBytes records per sampled tile
   uint8_t* tile_flags;            // [B*H][ceil(N/128)] tiles for the exact fallback
   // outputs
   int32_t* lsh;                   // [B][H][N][A]
   int32_t* nb;                    // [B][H][N][Wout]
   uint8_t* valid;                 // [B][H][N][Wout]
 };
+
+// Sample-pass record per sampled key tile in a row's buffer: 128 upper
+// score halves (256 bytes) and the tile's 128-bit candidate mask.
+constexpr int kSampleTileBytes = 272;
 
 // Index of the member mask of 64-key word w, round r, bucket u. The two words
 // of a 128-key tile are adjacent, so one tile's masks for all (round, bucket)

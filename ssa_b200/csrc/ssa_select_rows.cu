@@ -4,14 +4,14 @@
 //                   probe) slot and whether any of those buckets is empty.
 //   k_rows          warp per query row, after a scan pass of k_scan_tc:
 //     THRESH mode   from the sampled candidates, tau = the x-th largest score
-//                   (x ~ 2A scaled by the sampled fraction of key tiles): a
-//                   per-row threshold the full scan uses to keep only ~2A
-//                   candidates.
+//                   (x ~ 3A scaled by the sampled fraction of key tiles),
+//                   rounded down to its upper 16 bits: a per-row threshold
+//                   the full scan uses to keep only ~3A candidates.
 //     FINAL mode    verifies that at least A candidates reached tau (then
 //                   every top-A member did), adds the special keys (pad keys,
 //                   causal self, empty-bucket fallbacks) after replaying the
 //                   reference's slot order for each, selects the exact top-A
-//                   by a 4-pass radix select, and writes the merged neighbor
+//                   by range-narrowing histograms, and writes the merged neighbor
 //                   row (self, then ascending window/global/LSH keys) or the
 //                   LSH row in the reference's topk order. A row that fails
 //                   the verification, or overflowed its buffer, flags its
@@ -57,24 +57,28 @@ __global__ void __launch_bounds__(128) k_hash_queries(GraphDev g) {
 // Warp helpers
 // ---------------------------------------------------------------------------
 
-// The kth largest (1-based, kth <= n) of n 16-bit keys packed four to a
-// 64-bit word (entry i in bits 16*(i%4) of word i/4), read from global memory
-// by a 2-pass, 8-bit radix select. Warp-collective.
-__device__ uint32_t warp_radix_kth16(const unsigned long long* src, int n, int kth, uint32_t* hist) {
+// The kth largest 16-bit order key among the candidates of a row's sample:
+// ntiles records of kSampleTileBytes (128 upper score halves, then the 128-bit
+// candidate mask). 2-pass, 8-bit radix select; lane L reads scores 4L..4L+3
+// of each record. Warp-collective.
+__device__ uint32_t warp_sample_kth(const unsigned char* base, int ntiles, int kth, uint32_t* hist) {
   const int lane = threadIdx.x & 31;
-  const int nw = (n + 3) >> 2;
   uint32_t prefix = 0, pmask = 0;
   int need = kth;
   for (int shift = 8; shift >= 0; shift -= 8) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0;
     __syncwarp();
-    for (int w = lane; w < nw; w += 32) {
-      const unsigned long long e = __ldcs(src + w);
+    for (int jt = 0; jt < ntiles; ++jt) {
+      const unsigned char* tb = base + (size_t)jt * kSampleTileBytes;
+      const uint2 kv = *reinterpret_cast<const uint2*>(tb + 8 * lane);
+      const uint32_t mw = *reinterpret_cast<const uint32_t*>(tb + 256 + 4 * (lane >> 3));
+      const uint32_t m4 = (mw >> ((4 * lane) & 31)) & 0xFu;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const uint32_t u = (uint32_t)(e >> (16 * q)) & 0xFFFFu;
-        if (4 * w + q < n && (u & pmask) == prefix) atomicAdd(&hist[(u >> shift) & 255u], 1u);
+        const uint32_t h = ((q < 2 ? kv.x : kv.y) >> (16 * (q & 1))) & 0xFFFFu;
+        const uint32_t u = (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);  // okey of the upper half
+        if (((m4 >> q) & 1u) && (u & pmask) == prefix) atomicAdd(&hist[(u >> shift) & 255u], 1u);
       }
     }
     __syncwarp();
@@ -103,7 +107,7 @@ __device__ uint32_t warp_radix_kth16(const unsigned long long* src, int n, int k
       before += c[j];
     }
     const unsigned who = __ballot_sync(0xffffffffu, found_bin >= 0);
-    const int src_lane = __ffs(who) - 1;
+    const int src_lane = __ffs(who) - 1;  // exists: the sample holds at least kth candidates
     const int bin = __shfl_sync(0xffffffffu, found_bin, src_lane);
     const uint32_t fb = __shfl_sync(0xffffffffu, found_before, src_lane);
     need -= (int)fb;
@@ -286,8 +290,10 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g, int stage, int mode
     const int b = (int)(bh / g.H), h = (int)(bh % g.H);
     const int gk = h / g.rep;
     const int bg = b * g.n_kv + gk;
-    const int cnt_all = g.rcnt[row];
-    const int c = min(cnt_all, g.capg);
+    // Two scan groups (even / odd key tiles) each fill half of the buffer.
+    const int half_cap = g.capg >> 1;
+    const int cnt0 = g.rcnt[row * 2], cnt1 = g.rcnt[row * 2 + 1];
+    const int cnt_all = cnt0 + cnt1;
     const unsigned long long* bo = g.buf + row * g.capg;
     if (stage == 0) {
       // ---- THRESH: tau = x-th largest sampled score ----------------------
@@ -302,8 +308,9 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g, int stage, int mode
         // The sample holds the upper 16 bits of each score's order key, so
         // tau is rounded down to the lowest score sharing the x-th key: at
         // least x sampled scores are >= tau.
-        const int c16 = min(cnt_all, 4 * g.capg);
-        if (x >= 1 && c16 >= x) tau = okey_inv(warp_radix_kth16(bo, c16, x, S.hist) << 16);
+        const int fit = (int)((size_t)g.capg * 8 / kSampleTileBytes);
+        if (x >= 1 && cnt_all >= x && sampled <= fit)
+          tau = okey_inv(warp_sample_kth(reinterpret_cast<const unsigned char*>(bo), sampled, x, S.hist) << 16);
       }
       if (lane == 0) g.tau[row] = tau;
       __syncwarp();
@@ -313,12 +320,13 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g, int stage, int mode
     // ---- FINAL -------------------------------------------------------------
     const float tau = g.tau[row];
     const int ntq = (g.N + 127) / 128;
-    if (cnt_all > g.capg || (tau > -INFINITY && cnt_all < g.A)) {
+    if (cnt0 > half_cap || cnt1 > half_cap || (tau > -INFINITY && cnt_all < g.A)) {
       if (lane == 0) g.tile_flags[bh * ntq + n / 128] = 1;  // exact fallback for this tile
       continue;
     }
+    const int c = cnt_all;
     for (int i = lane; i < c; i += 32) {
-      const unsigned long long e = __ldcs(bo + i);  // read once
+      const unsigned long long e = __ldcs(bo + (i < cnt0 ? i : half_cap + i - cnt0));  // read once
       S.sc[i] = __uint_as_float((uint32_t)e);
       S.ky[i] = (uint16_t)(e >> 32);
     }

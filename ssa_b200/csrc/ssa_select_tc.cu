@@ -15,9 +15,10 @@
 //                      tcgen05.commit releases the K stage and publishes S.
 //   warps 0-3          thread per query row (TMEM lane = row): OR the row's
 //                      bucket masks for the tile, tcgen05.ld the row's 128
-//                      scores, and append the candidates to the row's global
-//                      buffer -- all of them in the sample pass (16-bit order
-//                      keys), those with score >= tau in the full pass.
+//                      scores, and write them to the row's global buffer: in
+//                      the sample pass the upper 16 bits of every score of
+//                      the tile plus its candidate masks, in the full pass the
+//                      (key, score) pairs of candidates with score >= tau.
 //
 // bf16 x bf16 products are exact in fp32, so tensor-core scores differ from
 // the reference's fp32 sums only by accumulation order (rescore ties).
@@ -37,7 +38,7 @@ namespace tc {
 
 constexpr int ROWS = 128;   // query rows per CTA (MMA M, TMEM lanes)
 constexpr int NKEY = 128;   // keys per tile (MMA N)
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;  // warps 0-7 epilogue (two groups), 8 TMA, 9 MMA
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -242,11 +243,12 @@ __host__ __device__ inline SmemPlan plan(int D, const GraphDev& g) {
 
 }  // namespace tc
 
-// Candidate scan. pass 0 (sample): key tiles 0, s, 2s, ... and every
-// candidate is kept; pass 1 (full): all key tiles, candidates with
-// score >= tau[row] are kept. Kept (score, key) pairs go to the row's slice of
-// the global buffer; the row's count goes to rcnt (a count above the buffer
-// capacity means overflow).
+// Candidate scan. pass 0 (sample): key tiles 0, s, 2s, ..., one record of
+// upper score halves and candidate masks per tile; pass 1 (full): all key
+// tiles, candidates with score >= tau[row] are kept as (key, score) pairs in
+// the half of the row's buffer that belongs to the tile's epilogue group.
+// rcnt[row][group] counts the candidates seen (pass 0) or kept (pass 1; above
+// half the buffer means overflow).
 template <int D>
 __global__ void __launch_bounds__(tc::THREADS, 2)
     k_scan_tc(GraphDev g, int pass, const __grid_constant__ CUtensorMap qmap,
@@ -268,11 +270,11 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
   uint64_t* kfull = bars;           // [NS] K stage loaded (TMA tx)
   uint64_t* kempty = bars + 4;      // [NS] K stage consumed (MMA commit)
   uint64_t* sfull = bars + 8;       // [2] S accumulator ready (MMA commit)
-  uint64_t* sempty = bars + 10;     // [2] S accumulator drained (4 epilogue warps)
+  uint64_t* sempty = bars + 10;     // [2] S accumulator drained (its group's 4 warps)
   uint64_t* qfull = bars + 12;      // q tile loaded
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 13);
   uint64_t* bfull = bars + 14;      // [NB_ST] mask block loaded (bulk tx)
-  uint64_t* bempty = bars + 18;     // [NB_ST] mask block read (4 epilogue warps)
+  uint64_t* bempty = bars + 18;     // [NB_ST] mask block read (the reading group's 4 warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + sp.tmem_slot);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -303,7 +305,7 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 5) {  // TMEM: 2 accumulators x NKEY fp32 columns
+  if (warp == 9) {  // TMEM: 2 accumulators x NKEY fp32 columns
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
                  "r"(2 * NKEY));
@@ -314,7 +316,7 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       mbar_expect_tx(qfull, ATOMS * ROWS * 128);
@@ -342,7 +344,7 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
       for (int i = max(0, issued - NS); i < issued; ++i) mbar_drain(kfull + i % NS, (i / NS) & 1);
       for (int i = max(0, issued_b - NB_ST); i < issued_b; ++i) mbar_drain(bfull + i % NB_ST, (i / NB_ST) & 1);
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && mbar_wait(qfull, 0, abort_flag, 13)) {
       const uint32_t qa = smem_u32(qs);
@@ -365,20 +367,26 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    const int t = threadIdx.x;  // row within the tile; TMEM lane
+    // Group grp (warps 4*grp .. 4*grp+3) takes the tiles i with i % 2 == grp,
+    // i.e. accumulator grp; thread t of a group owns query row n0 + t (TMEM
+    // lane t). Each group appends to its own half of the row's buffer.
+    const int grp = warp >> 2;
+    const int t = (warp & 3) * 32 + lane;
     const int n = n0 + t;
     const bool act = n < g.N;
     const int64_t row = (int64_t)bh * g.N + n;
-    if (act)
+    if (act && grp == 0)
       for (int tt = 0; tt < g.NT; ++tt)
         toff[tt * ROWS + t] = (uint16_t)((tt / (1 + g.Te)) * g.NB + g.qids[row * g.NT + tt]);
+    asm volatile("bar.sync 1, 256;" ::: "memory");  // both groups see the offsets
     const float thr = (pass == 1 && act) ? g.tau[row] : -INFINITY;
-    unsigned long long* bo = g.buf + row * g.capg;
+    const int half_cap = g.capg >> 1;
+    unsigned long long* bo = g.buf + row * g.capg;      // sample records (pass 0)
+    unsigned long long* bh_out = bo + grp * half_cap;   // this group's half (pass 1)
     int cnt = 0;
-    unsigned long long pack = 0ull;  // sample pass: up to 3 pending entries
     const uint4* bmg4 = reinterpret_cast<const uint4*>(g.bmap + bmap_idx(g, bg, 0, 0, 0));
-    for (int i = 0; i < ntl; ++i) {
-      const int sb = i & 1;
+    for (int i = grp; i < ntl; i += 2) {
+      const int sb = grp;
       const int kt = i * step;
       const int key0 = kt * NKEY;
       // Candidate masks first: they overlap the wait for S. Each (round,
@@ -419,66 +427,69 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
       }
       if (!mbar_wait_warp(sfull + sb, (i >> 1) & 1, abort_flag, 16)) break;
       tc_fence_after();
-      const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + sb * NKEY;
+      const uint32_t ta = tmem + ((uint32_t)((warp & 3) * 32) << 16) + sb * NKEY;
+      unsigned char* tdst = reinterpret_cast<unsigned char*>(bo) + (size_t)i * kSampleTileBytes;
+      const bool rec = pass == 0 && act && (size_t)(i + 1) * kSampleTileBytes <= (size_t)g.capg * 8;
 #pragma unroll
-      for (int hw = 0; hw < 2; ++hw) {
-        float sc[64];
-        tmem_ld32(ta + hw * 64, sc);
-        tmem_ld32(ta + hw * 64 + 32, sc + 32);
+      for (int c = 0; c < 4; ++c) {  // 32-column chunks
+        float sc[32];
+        tmem_ld32(ta + c * 32, sc);
         tmem_wait_ld();
-        if (hw == 1) {  // the accumulator can be reused once both halves are read
+        if (c == 3) {  // the accumulator can be reused once all columns are read
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(sempty + sb);
         }
+        const uint32_t cm = (uint32_t)(w[c >> 1] >> ((c & 1) * 32));
+        if (pass == 0) {
+          // Sample pass: the upper 16 bits of all 32 scores (two per 32-bit
+          // word, no compaction); the tile's candidate masks follow the 256
+          // score bytes. The threshold stage reads the masks.
+          if (rec) {
+            uint4* dst = reinterpret_cast<uint4*>(tdst + c * 64);
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const uint32_t cm = (uint32_t)(w[hw] >> (c * 32));
-          if (!cm) continue;
-          const uint32_t kbase32 = (uint32_t)(key0 + hw * 64 + c * 32);
-          if (pass == 0) {
-            // Sample pass: every candidate's 16-bit order-key prefix, packed
-            // four to a 64-bit store (the threshold needs no keys).
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if ((cm >> j) & 1u) {
-                pack |= (unsigned long long)(okey(sc[c * 32 + j]) >> 16) << (16 * (cnt & 3));
-                ++cnt;
-                if ((cnt & 3) == 0) {
-                  if (cnt <= 4 * g.capg) bo[(cnt >> 2) - 1] = pack;
-                  pack = 0ull;
-                }
-              }
+            for (int v = 0; v < 4; ++v) {
+              uint4 o;
+              o.x = __byte_perm(__float_as_uint(sc[8 * v + 0]), __float_as_uint(sc[8 * v + 1]), 0x7632);
+              o.y = __byte_perm(__float_as_uint(sc[8 * v + 2]), __float_as_uint(sc[8 * v + 3]), 0x7632);
+              o.z = __byte_perm(__float_as_uint(sc[8 * v + 4]), __float_as_uint(sc[8 * v + 5]), 0x7632);
+              o.w = __byte_perm(__float_as_uint(sc[8 * v + 6]), __float_as_uint(sc[8 * v + 7]), 0x7632);
+              dst[v] = o;
             }
-            continue;
           }
-          uint32_t h0 = 0, h1 = 0, h2 = 0, h3 = 0;
+          continue;
+        }
+        if (!cm) continue;
+        const uint32_t kbase32 = (uint32_t)(key0 + c * 32);
+        uint32_t h0 = 0, h1 = 0, h2 = 0, h3 = 0;
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            h0 |= (sc[c * 32 + j] >= thr ? 1u : 0u) << j;
-            h1 |= (sc[c * 32 + j + 1] >= thr ? 2u : 0u) << j;
-            h2 |= (sc[c * 32 + j + 2] >= thr ? 4u : 0u) << j;
-            h3 |= (sc[c * 32 + j + 3] >= thr ? 8u : 0u) << j;
-          }
-          uint32_t hit = (h0 | h1 | h2 | h3) & cm;
-          while (hit) {
-            const int j = __ffs(hit) - 1;
-            hit &= hit - 1;
-            if (cnt < g.capg)
-              bo[cnt] = ((unsigned long long)(kbase32 + j) << 32) | __float_as_uint(pick32(sc + c * 32, j));
-            ++cnt;
-          }
+        for (int j = 0; j < 32; j += 4) {
+          h0 |= (sc[j] >= thr ? 1u : 0u) << j;
+          h1 |= (sc[j + 1] >= thr ? 2u : 0u) << j;
+          h2 |= (sc[j + 2] >= thr ? 4u : 0u) << j;
+          h3 |= (sc[j + 3] >= thr ? 8u : 0u) << j;
+        }
+        uint32_t hit = (h0 | h1 | h2 | h3) & cm;
+        while (hit) {
+          const int j = __ffs(hit) - 1;
+          hit &= hit - 1;
+          if (cnt < half_cap)
+            bh_out[cnt] = ((unsigned long long)(kbase32 + j) << 32) | __float_as_uint(pick32(sc, j));
+          ++cnt;
         }
       }
+      if (pass == 0) {
+        if (rec)
+          *reinterpret_cast<uint4*>(tdst + 256) =
+              make_uint4((uint32_t)w[0], (uint32_t)(w[0] >> 32), (uint32_t)w[1], (uint32_t)(w[1] >> 32));
+        cnt += __popcll(w[0]) + __popcll(w[1]);
+      }
     }
-    if (act) {
-      if (pass == 0 && (cnt & 3) && cnt <= 4 * g.capg) bo[cnt >> 2] = pack;
-      g.rcnt[row] = cnt;
-    }
+    if (act) g.rcnt[row * 2 + grp] = cnt;
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * NKEY));
   }
