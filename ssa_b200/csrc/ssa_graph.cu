@@ -42,7 +42,7 @@ namespace ssa {
 // ---------------------------------------------------------------------------
 // 1. Key hashing + bucket membership masks
 // ---------------------------------------------------------------------------
-template <int DT>
+template <int DT, int D>
 __global__ void __launch_bounds__(256) k_hash_keys(GraphDev g) {
   extern __shared__ __align__(16) float s_planes[];  // R * p * d
   const int bg = blockIdx.y;
@@ -59,19 +59,29 @@ __global__ void __launch_bounds__(256) k_hash_keys(GraphDev g) {
   if (!act) return;
   const int lane = threadIdx.x & 31;
   const int wbase = m - lane;  // multiple of 32
+  // The key row stays in registers for all R * p projections.
+  float x[D];
   const void* row = row_ptr<DT>(g.k, b * g.k_sb + gk * g.k_sh + (int64_t)m * g.k_sm);
+#pragma unroll
+  for (int i = 0; i < D; i += 4) {
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < g.d) v = load4<DT>(row, i);
+    x[i] = v.x; x[i + 1] = v.y; x[i + 2] = v.z; x[i + 3] = v.w;
+  }
   for (int r = 0; r < g.R; ++r) {
     uint32_t code = 0;
     for (int j = 0; j < g.p; ++j) {
       const float* pl = s_planes + (r * g.p + j) * g.d;
       float s0 = 0.f, s1 = 0.f;
-      for (int t = 0; t < g.d; t += 4) {
-        const float4 x = load4<DT>(row, t);
-        const float4 w = *reinterpret_cast<const float4*>(pl + t);
-        s0 = fmaf(x.x, w.x, s0);
-        s1 = fmaf(x.y, w.y, s1);
-        s0 = fmaf(x.z, w.z, s0);
-        s1 = fmaf(x.w, w.w, s1);
+#pragma unroll
+      for (int t = 0; t < D; t += 4) {
+        if (t < g.d) {
+          const float4 w = *reinterpret_cast<const float4*>(pl + t);
+          s0 = fmaf(x[t], w.x, s0);
+          s1 = fmaf(x[t + 1], w.y, s1);
+          s0 = fmaf(x[t + 2], w.z, s0);
+          s1 = fmaf(x[t + 3], w.w, s1);
+        }
       }
       if (s0 + s1 > 0.f) code |= 1u << j;  // proj > 0, strict (:589)
     }
@@ -478,13 +488,10 @@ cudaError_t launch_graph(const GraphDev& g, int mode, cudaStream_t st) {
   {
     const size_t sm = (size_t)g.R * g.p * g.d * sizeof(float);
     dim3 grid((g.M + 255) / 256, g.B * g.n_kv);
-    if (g.dtype == kDtF32) {
-      if ((e = set_smem(k_hash_keys<kDtF32>, sm)) != cudaSuccess) return e;
-      k_hash_keys<kDtF32><<<grid, 256, sm, st>>>(g);
-    } else {
-      if ((e = set_smem(k_hash_keys<kDtBF16>, sm)) != cudaSuccess) return e;
-      k_hash_keys<kDtBF16><<<grid, 256, sm, st>>>(g);
-    }
+    auto fn = g.dtype == kDtF32 ? (g.d <= 64 ? k_hash_keys<kDtF32, 64> : k_hash_keys<kDtF32, 128>)
+                                : (g.d <= 64 ? k_hash_keys<kDtBF16, 64> : k_hash_keys<kDtBF16, 128>);
+    if ((e = set_smem(fn, sm)) != cudaSuccess) return e;
+    fn<<<grid, 256, sm, st>>>(g);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   k_bucket_trim<<<g.B * g.n_kv * g.R, 256, 0, st>>>(g);

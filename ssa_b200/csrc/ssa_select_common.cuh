@@ -157,11 +157,15 @@ __device__ __forceinline__ float dot_row_global(const float* q, const void* row,
 // sparse_attention.py:559-597; step-wise multi-probe, :599-646: probe t flips
 // the bit with the t-th smallest |proj| of the ORIGINAL id, ties in plane
 // order). Returns whether any of those buckets is empty.
+// Bucket ids of one row (q in registers) for every (round, probe) slot:
+// tids[(r * (1 + Te) + probe) * rows + t]; returns whether any of those
+// buckets is empty. Hyperplane j of round r is rp + (r * max_p + j) * d.
 template <int D>
-__device__ inline bool hash_row_ids(const GraphDev& g, const float* q, int bg, uint16_t* tids, int rows,
-                                    int t) {
+__device__ inline bool hash_row_ids(const GraphDev& g, const float* q, int bg, uint16_t* tids, int rows, int t) {
   for (int r = 0; r < g.R; ++r) {
-    float proj[12];
+    float proj[12];  // registers: written and read with static indices only
+#pragma unroll
+    for (int j = 0; j < 12; ++j) proj[j] = 0.f;
     uint32_t id = 0;
     for (int j = 0; j < g.p; ++j) {
       const float* pl = g.rp + ((int64_t)r * g.max_p + j) * g.d;
@@ -177,18 +181,24 @@ __device__ inline bool hash_row_ids(const GraphDev& g, const float* q, int bg, u
         }
       }
       const float s = s0 + s1;
-      proj[j] = s;
       if (s > 0.f) id |= 1u << j;
+      if (g.Te > 0) {
+#pragma unroll
+        for (int jj = 0; jj < 12; ++jj)
+          if (jj == j) proj[jj] = s;
+      }
     }
     tids[(r * (1 + g.Te)) * rows + t] = (uint16_t)id;
     uint32_t used = 0;
     for (int tt = 0; tt < g.Te; ++tt) {
       int best = -1;
       float bmag = 0.f;
-      for (int j = 0; j < g.p; ++j) {
-        if ((used >> j) & 1u) continue;
-        const float a = fabsf(proj[j]);
-        if (best < 0 || a < bmag) { best = j; bmag = a; }
+#pragma unroll
+      for (int j = 0; j < 12; ++j) {
+        if (j < g.p && !((used >> j) & 1u)) {
+          const float a = fabsf(proj[j]);
+          if (best < 0 || a < bmag) { best = j; bmag = a; }
+        }
       }
       used |= 1u << best;
       tids[(r * (1 + g.Te) + 1 + tt) * rows + t] = (uint16_t)(id ^ (1u << best));
