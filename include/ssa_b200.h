@@ -164,6 +164,30 @@ SSA_API int ssa_attn_bwd(const ssa_attn_params* p, const void* q, const void* k,
                  void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
                  void* stream);
 
+/*
+ * ssa_attn_bwd without a workspace argument -- no counterpart in the
+ * reference, which allocates through PyTorch. For callers that cannot
+ * allocate device memory: a host binding that only receives device buffers
+ * from elsewhere and has no device allocator of its own, or a process whose
+ * device memory footprint is fixed after set-up. The scratch is a file-scope
+ * device array of SSA_ATTN_BWD_STATIC_SCRATCH_BYTES (64 MiB) per device, so
+ * the call allocates nothing; problems whose scratch
+ * (ssa_attn_bwd_workspace_size) exceeds it are rejected with
+ * SSA_ERR_WORKSPACE, about 2.5 million edges (B*H*N*Kn) at most.
+ *   - The first call on each device resolves the array's address with
+ *     cudaGetSymbolAddress; make that first call before any stream capture.
+ *   - Nothing in the scratch has to start at zero.
+ *   - Calls share the device's one array: two calls whose executions overlap
+ *     (other streams, or host threads without ordering between them) race on
+ *     it and corrupt each other's results. Serialise them on one stream.
+ * Arguments and results are those of ssa_attn_bwd.
+ */
+#define SSA_ATTN_BWD_STATIC_SCRATCH_BYTES (64u << 20)
+SSA_API int ssa_attn_bwd_noalloc(const ssa_attn_params* p, const void* q, const void* k,
+                                 const void* v, const void* nb, const uint8_t* valid,
+                                 const void* dO, const float* lse, void* dq, void* dk, void* dv,
+                                 void* stream);
+
 /* Error code recorded by a kernel whose bounded wait on an on-chip barrier
  * ran out (0 = none); synchronises with the device. clear != 0 resets it. */
 SSA_API int32_t ssa_device_error(int32_t clear);

@@ -15,6 +15,9 @@ LIB_PATH = os.path.join(PKG, "libssa_b200.so")
 
 SSA_OK, SSA_ERR_INVALID, SSA_ERR_UNSUPPORTED, SSA_ERR_WORKSPACE, SSA_ERR_CUDA, SSA_ERR_DEVICE = range(6)
 SSA_F32, SSA_BF16 = 0, 1
+# Size of the static device scratch of ssa_attn_bwd_noalloc (the header's
+# SSA_ATTN_BWD_STATIC_SCRATCH_BYTES).
+SSA_ATTN_BWD_STATIC_SCRATCH_BYTES = 64 << 20
 
 _i32 = ctypes.c_int32
 _i64 = ctypes.c_int64
@@ -55,6 +58,8 @@ SIGNATURES = {
     "ssa_attn_bwd_workspace_size": (_sz, [ctypes.POINTER(AttnParams)]),
     "ssa_attn_bwd": (ctypes.c_int, [ctypes.POINTER(AttnParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                     _vp, _vp, _vp, _vp, _sz, _vp]),
+    "ssa_attn_bwd_noalloc": (ctypes.c_int, [ctypes.POINTER(AttnParams), _vp, _vp, _vp, _vp, _vp, _vp,
+                                            _vp, _vp, _vp, _vp, _vp]),
     "ssa_device_error": (_i32, [_i32]),
     "ssa_last_error": (ctypes.c_char_p, []),
     "ssa_abi_version": (_i32, []),

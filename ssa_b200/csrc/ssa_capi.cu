@@ -7,6 +7,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "../../include/ssa_b200.h"
 #include "ssa_common.cuh"
 #include "ssa_internal.h"
@@ -273,6 +275,72 @@ int ssa_attn_bwd(const ssa_attn_params* p, const void* q, const void* k, const v
   a.dq = dq; a.dk = dk; a.dv = dv;
   cudaError_t e = ssa::launch_attn_bwd(a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attention backward launch");
+  return SSA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Attention backward without a caller workspace: the scratch is a file-scope
+// device array, one per device, whose address the host resolves once.
+// ---------------------------------------------------------------------------
+}  // extern "C"
+
+namespace {
+// Nothing in it has to start at zero: k_attn_bwd_rows writes every edge entry
+// (weight, dS, sort key, id) before the sort reads it, and the sort's
+// temporaries need no initial value.
+__device__ __align__(256) unsigned char g_attn_bwd_scratch[SSA_ATTN_BWD_STATIC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+// Address of this device's scratch array: cudaGetSymbolAddress on the first
+// call per device (which may also load the module), cached afterwards.
+int scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(SSA_ERR_UNSUPPORTED, "device ordinal %d >= %d", dev, kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_attn_bwd_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static attention-backward scratch)");
+    g_scratch_addr[dev] = ptr;
+  }
+  *out = g_scratch_addr[dev];
+  return SSA_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int ssa_attn_bwd_noalloc(const ssa_attn_params* p, const void* q, const void* k, const void* v,
+                         const void* nb, const uint8_t* valid, const void* dO, const float* lse,
+                         void* dq, void* dk, void* dv, void* stream) {
+  int rc;
+  if ((rc = check_attn(p, q, k, v, nb, valid))) return rc;
+  if ((rc = check_rows("dO", dO, p->dtype, p->d, p->o_sb, p->o_sh, p->o_sn))) return rc;
+  if ((rc = check_rows("dq", dq, p->dtype, p->d, p->o_sb, p->o_sh, p->o_sn))) return rc;
+  if (!lse || !dk || !dv) return fail(SSA_ERR_INVALID, "lse/dk/dv are NULL");
+  const int64_t E = (int64_t)p->B * p->H * p->N * p->Kn;
+  if (E >= (int64_t(1) << 31)) return fail(SSA_ERR_UNSUPPORTED, "too many edges (%lld)", (long long)E);
+  if ((int64_t)p->B * p->n_kv * p->M >= (int64_t(1) << 31))
+    return fail(SSA_ERR_UNSUPPORTED, "B * n_kv * M too large");
+  ssa::AttnDev a = attn_dev(p);
+  const size_t need = ssa::attn_bwd_workspace_layout(a, nullptr, nullptr);
+  if (need > (size_t)SSA_ATTN_BWD_STATIC_SCRATCH_BYTES)
+    return fail(SSA_ERR_WORKSPACE,
+                "ssa_attn_bwd_noalloc: this problem needs %zu bytes of scratch but the static scratch "
+                "holds %zu (B*H*N*Kn = %lld edges); call ssa_attn_bwd with a caller workspace instead",
+                need, (size_t)SSA_ATTN_BWD_STATIC_SCRATCH_BYTES, (long long)E);
+  void* scratch = nullptr;
+  if ((rc = scratch_address(&scratch))) return rc;
+  ssa::attn_bwd_workspace_layout(a, &a, scratch);
+  a.q = q; a.k = k; a.v = v; a.nb = nb; a.valid = valid; a.dO = dO; a.lse_in = lse;
+  a.dq = dq; a.dk = dk; a.dv = dv;
+  cudaError_t e = ssa::launch_attn_bwd(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attention backward launch (static scratch)");
   return SSA_OK;
 }
 

@@ -118,6 +118,12 @@ def test_library_exports_every_declared_symbol():
     assert L.ssa_abi_version() == 100
 
 
+def test_static_scratch_size_matches_header():
+    m = re.search(r"#define SSA_ATTN_BWD_STATIC_SCRATCH_BYTES \((\d+)u << (\d+)\)", open(HEADER).read())
+    assert m, "SSA_ATTN_BWD_STATIC_SCRATCH_BYTES not found in the header"
+    assert int(m.group(1)) << int(m.group(2)) == _lib.SSA_ATTN_BWD_STATIC_SCRATCH_BYTES
+
+
 def test_ctypes_layouts_match_header(tmp_path):
     src = tmp_path / "layout.c"
     fields_g = [f for f, _ in _lib.GraphParams._fields_]
