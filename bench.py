@@ -160,7 +160,7 @@ def run_gpu(args):
     import torch
     import torch.distributed as dist
 
-    from ssa_b200 import ops
+    from ssa_b200 import _lib, ops
     from ssa_b200.workloads import WORKLOADS, make_module, make_x, project
 
     world, rank, local = dist_info()
@@ -199,6 +199,7 @@ def run_gpu(args):
         clocks = ClockSampler(local)
         clocks.start()
         torch.cuda.synchronize()
+        launches0 = _lib.load().ssa_kernel_launches()
         evs = []
         for _ in range(args.steps):
             flush.zero_()
@@ -209,6 +210,7 @@ def run_gpu(args):
             e2.record(stream)
             evs.append((e0, e1, e2))
         torch.cuda.synchronize()
+        launches = _lib.load().ssa_kernel_launches() - launches0
         if world > 1:
             dist.barrier()
         clk = clocks.stop()
@@ -249,7 +251,6 @@ def run_gpu(args):
             val, _full = cpu_baseline_value(w, dt, args.baseline_slices)
             cpu = {"value": val, "unit": "tokens/s", "cores": cores, "kind": "port",
                    "sample": desc, "sample_seconds": round(dt, 3)}
-        launches_per_step = 4  # k_hash_keys, k_bucket_trim, k_select_merge, k_attn_fwd
         result = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -266,8 +267,9 @@ def run_gpu(args):
                          "algorithmic_bytes": alg_bytes},
             "step_roofline": {"achieved": step_gbs, "frac": step_gbs / peak, "unit": "GB/s",
                               "note": "attention algorithmic bytes over graph build + attention"},
-            "kernels_ms": {"graph_build": ms_graph, "attention": ms_attn},
-            "gpu_launches": launches_per_step * args.steps,
+            "kernels_ms": {"graph_build": ms_graph, "attention": ms_attn,
+                           "graph_build_per_step": [round(x, 3) for x in graph]},
+            "gpu_launches": launches,
             "clocks": clk,
             "e2e": e2e,
             "cpu_baseline": cpu,

@@ -195,6 +195,11 @@ SSA_API int32_t ssa_device_error(int32_t clear);
 /* Human-readable text for the last error on this host thread. */
 SSA_API const char* ssa_last_error(void);
 
+/* Number of kernel launches this library has issued in this process (a
+ * host-side count; library calls such as the CUB sort inside ssa_attn_bwd
+ * are not included). */
+SSA_API int64_t ssa_kernel_launches(void);
+
 /* ABI version of this library (major * 100 + minor). */
 SSA_API int32_t ssa_abi_version(void);
 

@@ -63,6 +63,7 @@ SIGNATURES = {
     "ssa_device_error": (_i32, [_i32]),
     "ssa_last_error": (ctypes.c_char_p, []),
     "ssa_abi_version": (_i32, []),
+    "ssa_kernel_launches": (_i64, []),
 }
 
 _lib = None

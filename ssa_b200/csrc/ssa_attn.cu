@@ -325,6 +325,7 @@ static cudaError_t fwd_t(const AttnDev& a, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   const int64_t rows = (int64_t)a.B * a.H * a.N;
   fn<<<(unsigned)((rows + 7) / 8), 256, smem, st>>>(a);
+  note_launch();
   return cudaGetLastError();
 }
 
@@ -382,6 +383,7 @@ static cudaError_t bwd_rows_t(const AttnDev& a, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   const int64_t rows = (int64_t)a.B * a.H * a.N;
   fn<<<(unsigned)((rows + 7) / 8), 256, smem, st>>>(a);
+  note_launch();
   return cudaGetLastError();
 }
 
@@ -409,10 +411,10 @@ static cudaError_t bwd_d(const AttnDev& a, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   const int64_t keys = (int64_t)a.B * a.n_kv * a.M;
   const unsigned grid = (unsigned)((keys + 7) / 8);
-  if (a.d <= 32) k_dkdv<DT, 1><<<grid, 256, 0, st>>>(a, E);
-  else if (a.d <= 64) k_dkdv<DT, 2><<<grid, 256, 0, st>>>(a, E);
-  else if (a.d <= 128) k_dkdv<DT, 4><<<grid, 256, 0, st>>>(a, E);
-  else k_dkdv<DT, 8><<<grid, 256, 0, st>>>(a, E);
+  if (a.d <= 32) { k_dkdv<DT, 1><<<grid, 256, 0, st>>>(a, E); note_launch(); }
+  else if (a.d <= 64) { k_dkdv<DT, 2><<<grid, 256, 0, st>>>(a, E); note_launch(); }
+  else if (a.d <= 128) { k_dkdv<DT, 4><<<grid, 256, 0, st>>>(a, E); note_launch(); }
+  else { k_dkdv<DT, 8><<<grid, 256, 0, st>>>(a, E); note_launch(); }
   return cudaGetLastError();
 }
 

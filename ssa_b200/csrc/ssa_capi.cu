@@ -7,6 +7,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "../../include/ssa_b200.h"
@@ -115,11 +116,16 @@ int check_select_fits(const ssa::GraphDev& g) {
 
 }  // namespace
 
+namespace ssa {
+static std::atomic<long long> g_kernel_launches{0};
+void note_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
+}  // namespace ssa
+
 extern "C" {
 
 const char* ssa_last_error(void) { return g_err; }
 
-int32_t ssa_abi_version(void) { return 100; }
+int32_t ssa_abi_version(void) { return 101; }
 
 int32_t ssa_device_error(int32_t clear) { return ssa::read_device_error(clear); }
 
@@ -282,6 +288,8 @@ int ssa_attn_bwd(const ssa_attn_params* p, const void* q, const void* k, const v
 // Attention backward without a caller workspace: the scratch is a file-scope
 // device array, one per device, whose address the host resolves once.
 // ---------------------------------------------------------------------------
+int64_t ssa_kernel_launches(void) { return ssa::g_kernel_launches.load(std::memory_order_relaxed); }
+
 }  // extern "C"
 
 namespace {

@@ -466,6 +466,7 @@ static cudaError_t launch_select_t(const GraphDev& g, int mode, int rows, size_t
   if (e != cudaSuccess) return e;
   dim3 grid((g.N + rows - 1) / rows, g.B * g.H);
   fn<<<grid, rows, smem, st>>>(g, mode);
+  note_launch();
   return cudaGetLastError();
 }
 
@@ -492,9 +493,11 @@ cudaError_t launch_graph(const GraphDev& g, int mode, cudaStream_t st) {
                                 : (g.d <= 64 ? k_hash_keys<kDtBF16, 64> : k_hash_keys<kDtBF16, 128>);
     if ((e = set_smem(fn, sm)) != cudaSuccess) return e;
     fn<<<grid, 256, sm, st>>>(g);
+    note_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   k_bucket_trim<<<g.B * g.n_kv * g.R, 256, 0, st>>>(g);
+  note_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   GraphDev f = g;
   if (g.use_tc && select_tc_pointers_ok(g)) {
@@ -519,6 +522,7 @@ cudaError_t launch_merge(const MergeDev& m, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   const int64_t total = (int64_t)m.B * m.H * m.N;
   k_merge_rows<<<(unsigned)((total + rows - 1) / rows), rows, bytes(rows), st>>>(m);
+  note_launch();
   return cudaGetLastError();
 }
 
@@ -531,6 +535,7 @@ cudaError_t launch_hash_ids(const void* x, int dtype, int B, int heads, int rows
     k_hash_ids<kDtF32><<<grid, 256, 0, st>>>(x, B, heads, rows, d, sb, sh, sn, rp, R, max_p, p, out);
   else
     k_hash_ids<kDtBF16><<<grid, 256, 0, st>>>(x, B, heads, rows, d, sb, sh, sn, rp, R, max_p, p, out);
+  note_launch();
   return cudaGetLastError();
 }
 

@@ -54,6 +54,9 @@ __host__ __device__ inline int64_t bmap_idx(const GraphDev& g, int bg, int w, in
   return ((((int64_t)bg * (g.Wpad >> 1) + (w >> 1)) * g.R + r) * g.NB + u) * 2 + (w & 1);
 }
 
+// Host-side count of kernel launches made by this library (ssa_kernel_launches).
+void note_launch();
+
 // Fills the workspace pointers of g (g->ws may be null to only size it) and
 // returns the bytes needed. Decides g->use_tc from the shapes.
 size_t graph_workspace_layout(GraphDev* g);

@@ -672,10 +672,12 @@ cudaError_t launch_hash_queries(const GraphDev& g, cudaStream_t st) {
     auto fn = g.dtype == kDtF32 ? k_hash_queries<kDtF32, 64> : k_hash_queries<kDtBF16, 64>;
     if ((e = smem_attr(fn, sm)) != cudaSuccess) return e;
     fn<<<grid, 128, sm, st>>>(g);
+    note_launch();
   } else {
     auto fn = g.dtype == kDtF32 ? k_hash_queries<kDtF32, 128> : k_hash_queries<kDtBF16, 128>;
     if ((e = smem_attr(fn, sm)) != cudaSuccess) return e;
     fn<<<grid, 128, sm, st>>>(g);
+    note_launch();
   }
   return cudaGetLastError();
 }
@@ -701,6 +703,7 @@ cudaError_t launch_rows(const GraphDev& g, int stage, int mode, cudaStream_t st)
   const int64_t resident = (int64_t)nsm * per_sm;
   if (blocks > resident) blocks = resident;
   fn<<<(unsigned)blocks, kWarps * 32, sm, st>>>(g, stage, mode);
+  note_launch();
   return cudaGetLastError();
 }
 

@@ -557,6 +557,7 @@ static cudaError_t launch_scan_t(const GraphDev& g, int pass, const CUtensorMap&
   if (e != cudaSuccess) return e;
   dim3 grid((g.N + tc::ROWS - 1) / tc::ROWS, g.B * g.H);
   fn<<<grid, tc::THREADS, sp.total, st>>>(g, pass, qmap, kmap);
+  note_launch();
   return cudaGetLastError();
 }
 
