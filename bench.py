@@ -50,6 +50,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the workload's batch size (profiling a smaller case)")
+    ap.add_argument("--shard", default="auto", choices=["auto", "groups", "rows"],
+                    help="multi-GPU partitioning (auto: query rows for c3, (batch, kv-head) groups otherwise)")
     ap.add_argument("--baseline-slices", type=int, default=2,
                     help="(batch, kv-group) slices in the CPU baseline sample")
     return ap.parse_args(argv)
@@ -156,12 +158,80 @@ def cpu_baseline_value(w, dt, slices):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+def _plan(args, w, world):
+    if args.shard != "auto":
+        return args.shard if world > 1 else "single"
+    if world == 1:
+        return "single"
+    return "rows" if w.B * w.n_kv < world or w.name == "c3" else "groups"
+
+
+class _Job:
+    """One rank's share of the workload's step: device tensors plus a
+    step() that runs graph build + gather attention on them."""
+
+    def __init__(self, plan, w, m, dev, world, rank):
+        import torch
+        from ssa_b200.sharding import GroupSharded, RowSharded
+        from ssa_b200.workloads import make_x, project
+        self.plan, self.w, self.m, self.world, self.rank = plan, w, m, world, rank
+        self.causal = w.causal and not w.cross
+        x, kv = make_x(w, dev, seed=1)           # the same job on every rank
+        if plan == "rows":
+            if w.cross or w.B != 1:
+                raise SystemExit("query-row sharding is for one self-attention sequence (B=1)")
+            self.runner = RowSharded(m, w.N, world, rank, causal=self.causal)
+            r0, r1 = self.runner.rows
+            xl = x[:, r0:r1]
+            with torch.no_grad():
+                self.q = m.Wq(xl).view(w.B, r1 - r0, w.H, w.d).transpose(1, 2)
+                self.k_seq = m.Wk(xl).view(w.B, r1 - r0, w.n_kv, w.d).permute(1, 0, 2, 3).contiguous()
+                self.v_seq = m.Wv(xl).view(w.B, r1 - r0, w.n_kv, w.d).permute(1, 0, 2, 3).contiguous()
+            self.tokens_local = w.B * (r1 - r0)
+        else:
+            self.q, self.k, self.v = project(m, x, kv)
+            if plan == "groups":
+                self.runner = GroupSharded(m, world, rank, causal=w.causal, is_cross=w.cross)
+                self.slices = self.runner.slices(w.B, w.n_kv)
+                self.tokens_local = sum((s.b1 - s.b0) * (s.g1 - s.g0) for s in self.slices) * w.N // w.n_kv
+            else:
+                self.tokens_local = w.B * w.N
+        del x, kv
+
+    def step(self, stream, mark):
+        """Runs one step; records `mark` (a CUDA event) between the graph
+        build and the attention where the plan has a single such point."""
+        import torch
+        from ssa_b200 import ops
+        m, w = self.m, self.w
+        if self.plan == "single":
+            nb, valid = m._graph(self.q, self.k, w.M, self.causal, w.cross)
+            mark.record(stream)
+            out, _ = ops.attn_fwd(self.q, self.k, self.v, nb, valid, m.scale, False, want_lse=False)
+            return out
+        if self.plan == "rows":
+            k, v = self.runner.gather_kv(self.k_seq, self.v_seq)
+            nb, valid = m._graph(self.q, k, w.N, self.causal, False, q_row0=self.runner.rows[0])
+            mark.record(stream)
+            out, _ = ops.attn_fwd(self.q, k, v, nb, valid, m.scale, False, want_lse=False)
+            return out
+        rep = w.H // w.n_kv
+        from ssa_b200.sharding import slice_views
+        graphs = []
+        for s in self.slices:
+            qs, ks, vs = slice_views(self.q, self.k, self.v, s, rep)
+            graphs.append((qs, ks, vs) + tuple(m._graph(qs, ks, w.M, self.causal, w.cross)))
+        mark.record(stream)
+        return [ops.attn_fwd(qs, ks, vs, nb, valid, m.scale, False, want_lse=False)[0]
+                for qs, ks, vs, nb, valid in graphs]
+
+
 def run_gpu(args):
     import torch
     import torch.distributed as dist
 
-    from ssa_b200 import _lib, ops
-    from ssa_b200.workloads import WORKLOADS, make_module, make_x, project
+    from ssa_b200 import _lib
+    from ssa_b200.workloads import WORKLOADS, make_module
 
     world, rank, local = dist_info()
     if world != args.gpus:
@@ -174,25 +244,16 @@ def run_gpu(args):
     w = WORKLOADS[args.workload]
     if args.batch:
         w = type(w)(**{**w.__dict__, "B": args.batch})
+    plan = _plan(args, w, world)
     m = make_module(w, dev)
-    x, kv = make_x(w, dev, seed=1 + rank)
-    q, k, v = project(m, x, kv)
-    del x, kv
-    causal = w.causal and not w.cross
+    job = _Job(plan, w, m, dev, world, rank)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
-
-    def step():
-        nb, valid = m._graph(q, k, w.M, causal, w.cross)
-        e_mid = torch.cuda.Event(enable_timing=True)
-        e_mid.record(stream)
-        out, _ = ops.attn_fwd(q, k, v, nb, valid, m.scale, False, want_lse=False)
-        return out, e_mid
 
     with torch.no_grad():
         for _ in range(max(args.warmup, 0)):
             flush.zero_()
-            step()
+            job.step(stream, torch.cuda.Event())
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -204,9 +265,10 @@ def run_gpu(args):
         for _ in range(args.steps):
             flush.zero_()
             e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
             e2 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            out, e1 = step()
+            job.step(stream, e1)
             e2.record(stream)
             evs.append((e0, e1, e2))
         torch.cuda.synchronize()
@@ -219,21 +281,25 @@ def run_gpu(args):
     attn = [b.elapsed_time(c) for a, b, c in evs]
     ms = statistics.mean(tot)
     ms_graph, ms_attn = statistics.mean(graph), statistics.mean(attn)
+    launches_all = launches
     if world > 1:
         t = torch.tensor([ms, ms_graph, ms_attn], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, ms_graph, ms_attn = [float(x) for x in t.tolist()]
+        c = torch.tensor([launches], device=dev, dtype=torch.float64)
+        dist.all_reduce(c)
+        launches_all = int(c.item())
 
-    tokens = w.B * w.N
-    value = world * tokens / (ms / 1e3)
+    tokens = w.B * w.N                      # the whole job, split over the ranks
+    value = tokens / (ms / 1e3)
     peak, peak_src = hbm_peak()
-    alg_bytes = w.bytes_per_token() * tokens
+    alg_bytes = w.bytes_per_token() * job.tokens_local   # this rank's attention bytes
     attn_gbs = alg_bytes / (ms_attn / 1e3) / 1e9
-    step_gbs = alg_bytes / (ms / 1e3) / 1e9
+    step_gbs = w.bytes_per_token() * tokens / (ms / 1e3) / 1e9 / world
     traffic = None
     try:
         with open(TRAFFIC_FILE) as f:
-            traffic = json.load(f).get(w.name, {}).get("k_attn_fwd")
+            traffic = json.load(f).get(w.name, {}).get("k_attn_fwd") if plan == "single" else None
     except Exception:
         pass
 
@@ -241,35 +307,37 @@ def run_gpu(args):
     # attention output back to pinned host memory, copies inside the timing.
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(args, m, w, q, k, v, dev, flush)
+        e2e = run_e2e(args, job, dev, flush, world)
 
     result = None
     if rank == 0:
         cpu = None
         if not args.no_cpu_baseline and world == 1:
-            dt, desc, cores = cpu_sample(w, m, q, k, v, args.baseline_slices)
+            dt, desc, cores = cpu_sample(w, m, job.q, job.k, job.v, args.baseline_slices)
             val, _full = cpu_baseline_value(w, dt, args.baseline_slices)
             cpu = {"value": val, "unit": "tokens/s", "cores": cores, "kind": "port",
                    "sample": desc, "sample_seconds": round(dt, 3)}
+        par = {"single": "one GPU, whole job",
+               "groups": f"group sharding: {w.B * w.n_kv} (batch, kv-head) units over {world} GPUs, no collective",
+               "rows": f"query-row sharding: {w.N // world} rows per GPU, K/V all-gathered (NCCL)"}[plan]
         result = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": w.dtype,
             "data": "synthetic (seeded N(0,1) activations; random-init weights in reference order)",
             "config": {"workload": w.name, "B": w.B, "N": w.N, "M": w.M, "H": w.H, "n_kv": w.n_kv,
                        "d_head": w.d, "K": w.K, "window": w.window, "R": w.R, "probes": w.T,
-                       "causal": w.causal, "cross": w.cross,
-                       "parallelism": f"weak: one full batch per GPU x{world}",
+                       "causal": w.causal, "cross": w.cross, "parallelism": par,
                        "l2": "flushed (256 MB write) between timed steps"},
             "roofline": {"kernel": "k_attn_fwd", "bound": "hbm", "achieved": attn_gbs, "peak": peak,
                          "unit": "GB/s", "frac": attn_gbs / peak, "traffic": traffic,
                          "peak_source": f"{peak_src} hbm_gbs",
                          "algorithmic_bytes": alg_bytes},
             "step_roofline": {"achieved": step_gbs, "frac": step_gbs / peak, "unit": "GB/s",
-                              "note": "attention algorithmic bytes over graph build + attention"},
+                              "note": "attention algorithmic bytes over graph build + attention, per GPU"},
             "kernels_ms": {"graph_build": ms_graph, "attention": ms_attn,
                            "graph_build_per_step": [round(x, 3) for x in graph]},
-            "gpu_launches": launches,
+            "gpu_launches": launches_all,
             "clocks": clk,
             "e2e": e2e,
             "cpu_baseline": cpu,
@@ -281,29 +349,59 @@ def run_gpu(args):
     return result
 
 
-def run_e2e(args, m, w, q, k, v, dev, flush):
+def run_e2e(args, job, dev, flush, world):
+    """The same step through the public API from pinned host memory: this
+    rank's inputs copied in, its outputs copied back, inside the timing."""
     import torch
-    qh = q.transpose(1, 2).contiguous().cpu().pin_memory()      # (B, N, H, d)
-    kh = k.transpose(1, 2).contiguous().cpu().pin_memory()      # (B, M, n_kv, d)
-    vh = v.transpose(1, 2).contiguous().cpu().pin_memory()
-    qd, kd, vd = torch.empty_like(qh, device=dev), torch.empty_like(kh, device=dev), torch.empty_like(vh, device=dev)
-    outh = torch.empty((w.B, w.H, w.N, w.d), dtype=q.dtype).pin_memory()
+    import torch.distributed as dist
+    from ssa_b200.sharding import slice_views
+    w, m = job.w, job.m
     stream = torch.cuda.current_stream(dev)
-    causal = w.causal and not w.cross
+
+    def pin(t):
+        return t.detach().contiguous().cpu().pin_memory()
+
+    if job.plan == "rows":
+        hosts = [pin(job.q.transpose(1, 2)), pin(job.k_seq), pin(job.v_seq)]    # (B,n,H,d), (m,B,n_kv,d)
+        outh = torch.empty((w.B, job.q.shape[2], w.H, w.d), dtype=job.q.dtype).pin_memory()
+    else:
+        blocks = job.slices if job.plan == "groups" else None
+        rep = w.H // w.n_kv
+        parts = []
+        for s in (blocks or [None]):
+            qs, ks, vs = (job.q, job.k, job.v) if s is None else slice_views(job.q, job.k, job.v, s, rep)
+            parts.append((pin(qs.transpose(1, 2)), pin(ks.transpose(1, 2)), pin(vs.transpose(1, 2))))
+        outs_h = [torch.empty(qh.shape, dtype=qh.dtype).pin_memory() for qh, _, _ in parts]
+    devs = None
 
     def one():
-        qd.copy_(qh, non_blocking=True)
-        kd.copy_(kh, non_blocking=True)
-        vd.copy_(vh, non_blocking=True)
-        q4, k4, v4 = qd.transpose(1, 2), kd.transpose(1, 2), vd.transpose(1, 2)
-        nb, valid = m.build_graph(q4, k4, w.N, w.M, w.B, dev, causal, w.cross)
-        out = m.apply_graph(q4, k4, v4, nb, valid)
-        outh.copy_(out, non_blocking=True)
+        nonlocal devs
+        if job.plan == "rows":
+            if devs is None:
+                devs = [torch.empty_like(h, device=dev) for h in hosts]
+            for d_, h in zip(devs, hosts):
+                d_.copy_(h, non_blocking=True)
+            q4 = devs[0].transpose(1, 2)
+            out = job.runner.step(q4, devs[1], devs[2])
+            outh.copy_(out.transpose(1, 2), non_blocking=True)
+            return
+        if devs is None:
+            devs = [[torch.empty_like(h, device=dev) for h in p] for p in parts]
+        for p, dp, oh in zip(parts, devs, outs_h):
+            for d_, h in zip(dp, p):
+                d_.copy_(h, non_blocking=True)
+            q4, k4, v4 = (t.transpose(1, 2) for t in dp)
+            Bs = q4.shape[0]
+            nb, valid = m.build_graph(q4, k4, w.N, w.M, Bs, dev, job.causal, w.cross)
+            out = m.apply_graph(q4, k4, v4, nb, valid)
+            oh.copy_(out.transpose(1, 2), non_blocking=True)
 
     with torch.no_grad():
         for _ in range(max(1, args.warmup)):
             one()
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         evs = []
         for _ in range(args.steps):
             flush.zero_()
@@ -315,11 +413,22 @@ def run_e2e(args, m, w, q, k, v, dev, flush):
             evs.append((a, b))
         torch.cuda.synchronize()
     ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
-    h2d = (qh.numel() + kh.numel() + vh.numel()) * qh.element_size()
-    d2h = outh.numel() * outh.element_size()
+    if job.plan == "rows":
+        h2d = sum(h.numel() * h.element_size() for h in hosts)
+        d2h = outh.numel() * outh.element_size()
+    else:
+        h2d = sum(h.numel() * h.element_size() for p in parts for h in p)
+        d2h = sum(o.numel() * o.element_size() for o in outs_h)
+    if world > 1:
+        t = torch.tensor([ms, float(h2d), float(d2h)], device=dev, dtype=torch.float64)
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t)
+        ms, h2d, d2h = float(mx[0]), int(t[1]), int(t[2])
+    api = ("RowSharded.step (NCCL all-gather of K/V + graph + attention)" if job.plan == "rows"
+           else "SparseAttention.build_graph + apply_graph (int64/bool graph contract)")
     return {"value": w.B * w.N / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "api": "SparseAttention.build_graph + apply_graph (int64/bool graph contract)"}
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": api}
 
 
 # ---------------------------------------------------------------------------
@@ -364,7 +473,7 @@ def run_reference(args):
     desc = desc.replace(f"{slices} of {w1.B * w1.n_kv}", f"{slices} of {w.B * w.n_kv}")
     res = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": full * 1e3,
-           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": w.dtype,
            "data": "synthetic", "config": {"workload": w.name, "B": w.B, "N": w.N, "H": w.H,
                                            "n_kv": w.n_kv, "K": w.K},
            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",

@@ -66,6 +66,12 @@ typedef struct {
   int32_t G;                /* number of global key indices */
   int64_t q_sb, q_sh, q_sn; /* element strides of q (B, H, N, d) */
   int64_t k_sb, k_sh, k_sm; /* element strides of k (B, n_kv, M, d) */
+  int32_t q_row0;           /* sequence position of query row 0 (0 unless the
+                             * queries are a slice of a longer sequence, e.g.
+                             * one rank's rows under query-row sharding): row i
+                             * is position q_row0 + i for the causal limit,
+                             * the window and the self slot */
+  int32_t reserved0;
 } ssa_graph_params;
 
 /* Neighbor-slot width of the merged graph: self + min(K-1, Kall) slots for

@@ -29,7 +29,8 @@ class GraphParams(ctypes.Structure):
     """ssa_graph_params."""
     _fields_ = [(n, _i32) for n in ("B", "H", "n_kv", "N", "M", "d", "dtype", "R", "max_p", "p_eff",
                                     "C", "T", "A", "causal", "is_cross", "K", "window", "G")] + \
-               [(n, _i64) for n in ("q_sb", "q_sh", "q_sn", "k_sb", "k_sh", "k_sm")]
+               [(n, _i64) for n in ("q_sb", "q_sh", "q_sn", "k_sb", "k_sh", "k_sm")] + \
+               [("q_row0", _i32), ("reserved0", _i32)]
 
 
 class AttnParams(ctypes.Structure):

@@ -323,15 +323,16 @@ class SparseAttention(nn.Module):
             self._glob_cache[key] = g
         return g
 
-    def _graph(self, q, k, M: int, causal: bool, is_cross: bool):
-        """Neighbor graph as int32 neighbors + uint8 valid (internal form)."""
+    def _graph(self, q, k, M: int, causal: bool, is_cross: bool, q_row0: int = 0):
+        """Neighbor graph as int32 neighbors + uint8 valid (internal form).
+        q_row0: sequence position of q's first row (query-row sharding)."""
         lsh = self.lsh_builder
         p_eff = lsh.compute_effective_p(M, lsh.C, lsh.max_P)
         A = lsh.output_width(M, self.lsh_k)
         return ops.build_graph(q, k, lsh.rand_proj, self._glob(M, q.device), R=lsh.R,
                                max_p=lsh.max_P, p_eff=p_eff, C=lsh.C, T=lsh.T, A=A,
                                causal=causal, is_cross=is_cross, K=self.K,
-                               window=self.config.window_size)
+                               window=self.config.window_size, q_row0=q_row0)
 
     def build_graph(self, q: torch.Tensor, k: torch.Tensor, N: int, M: int, B: int, device,
                     causal: bool, is_cross: bool) -> Tuple[torch.Tensor, torch.Tensor]:

@@ -71,6 +71,8 @@ int check_graph(const ssa_graph_params* p) {
     return fail(SSA_ERR_INVALID, "C, A, K >= 1 and T, window, G >= 0 required");
   if (p->M > (1 << 20)) return fail(SSA_ERR_UNSUPPORTED, "key length M=%d exceeds 2^20", p->M);
   if (p->N > (1 << 30)) return fail(SSA_ERR_UNSUPPORTED, "query length too large");
+  if (p->q_row0 < 0 || (int64_t)p->q_row0 + p->N > (int64_t(1) << 30))
+    return fail(SSA_ERR_INVALID, "q_row0=%d out of range", p->q_row0);
   if ((int64_t)p->B * p->H > 65535 || (int64_t)p->B * p->n_kv > 65535)
     return fail(SSA_ERR_UNSUPPORTED, "B*H must be <= 65535");
   if (p->is_cross && p->causal) return fail(SSA_ERR_INVALID, "cross-attention is never causal");
@@ -88,6 +90,7 @@ ssa::GraphDev dev_of(const ssa_graph_params* p) {
   g.W = (p->M + 63) / 64;
   g.Wpad = (g.W + 1) / 2 * 2;
   g.A = p->A; g.causal = p->causal; g.is_cross = p->is_cross; g.window = p->window; g.G = p->G;
+  g.row0 = p->q_row0;
   g.Wout = graph_width(p);
   g.q_sb = p->q_sb; g.q_sh = p->q_sh; g.q_sn = p->q_sn;
   g.k_sb = p->k_sb; g.k_sh = p->k_sh; g.k_sm = p->k_sm;
@@ -125,7 +128,7 @@ extern "C" {
 
 const char* ssa_last_error(void) { return g_err; }
 
-int32_t ssa_abi_version(void) { return 101; }
+int32_t ssa_abi_version(void) { return 102; }
 
 int32_t ssa_device_error(int32_t clear) { return ssa::read_device_error(clear); }
 

@@ -164,6 +164,7 @@ __global__ void k_select_merge(GraphDev g, int mode) {
   const int n = blockIdx.x * rows + t;
   const bool act = n < g.N;
   const int n_hi = min(g.N, (int)(blockIdx.x + 1) * rows) - 1;
+  const int na = g.row0 + n;  // sequence position of this row
 
   // Sorted unique globals for the merge (only the set matters to it).
   if (t == 0) {
@@ -201,7 +202,7 @@ __global__ void k_select_merge(GraphDev g, int mode) {
   // row's candidates (OR of its bucket masks) are scored.
   RowHeap<KT> heap{hs, hk, rows, t};
   int cnt = 0;
-  const int nkt = g.causal ? min(g.W, (n_hi >> 6) + 1) : g.W;
+  const int nkt = g.causal ? min(g.W, ((g.row0 + n_hi) >> 6) + 1) : g.W;
   const char* kbase = reinterpret_cast<const char*>(row_ptr<DT>(g.k, b * g.k_sb + gk * g.k_sh));
   for (int kt = 0; kt < nkt; ++kt) {
     const int key0 = kt * KTILE;
@@ -221,8 +222,8 @@ __global__ void k_select_merge(GraphDev g, int mode) {
       w |= __ldg(&g.bmap[bmap_idx(g, bg, kt, r, tids[tt * rows + t])]);
     }
     w &= ~__ldg(g.pmask + (int64_t)bg * g.Wpad + kt);
-    if (g.causal) {  // keys < n only; n itself is a special key
-      const int lim = n - key0;
+    if (g.causal) {  // keys < na only; na itself is a special key
+      const int lim = na - key0;
       if (lim <= 0) w = 0ull;
       else if (lim < 64) w &= (1ull << lim) - 1ull;
     }
@@ -243,7 +244,7 @@ __global__ void k_select_merge(GraphDev g, int mode) {
     }
   }
   if (!act) return;
-  finish_row<DT, D, KT>(g, mode, heap, cnt, tids, rows, t, gs, bh, b, h, gk, bg, n, any_empty);
+  finish_row<DT, D, KT>(g, mode, heap, cnt, tids, rows, t, gs, bh, b, h, gk, bg, n, na, any_empty);
 }
 
 // Standalone merge_neighbors (sparse_attention.py:966-1089) over explicit

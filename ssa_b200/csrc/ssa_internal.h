@@ -14,6 +14,7 @@ struct GraphDev {
   int B, H, n_kv, rep, N, M, d, dtype;
   int R, max_p, p, C, Te, NT, NB, W, Wpad, A;
   int causal, is_cross, window, G, Wout;
+  int row0;  // sequence position of query row 0 (query-row sharding)
   int64_t q_sb, q_sh, q_sn, k_sb, k_sh, k_sm;
   const void* q;
   const void* k;

@@ -108,6 +108,7 @@ __device__ __forceinline__ bool key_member(const GraphDev& g, int bg, int r, int
 // Replays the reference's slot order (round-major, primary bucket then
 // probes, slot c = 0..C-1) for one key x and reports whether x's FIRST slot
 // is valid -- the cross-round dedup rule of sparse_attention.py:884-890.
+// n is the query's sequence position.
 __device__ inline bool replay_first_valid(const GraphDev& g, const uint16_t* tids, int rows, int t,
                                           int bg, int n, int x) {
   for (int tt = 0; tt < g.NT; ++tt) {
@@ -221,13 +222,15 @@ __device__ inline bool hash_row_ids(const GraphDev& g, const float* q, int bg, u
 template <int DT, int D, typename KT>
 __device__ inline void finish_row(const GraphDev& g, int mode, RowHeap<KT>& heap, int& cnt,
                                   const uint16_t* tids, int rows, int t, const int32_t* gs, int bh,
-                                  int b, int h, int gk, int bg, int n, bool any_empty) {
+                                  int b, int h, int gk, int bg, int n, int na, bool any_empty) {
+  // n: the row within q and the outputs; na = g.row0 + n: its sequence
+  // position (causal limit, window, self).
   const char* kbase = reinterpret_cast<const char*>(row_ptr<DT>(g.k, b * g.k_sb + gk * g.k_sh));
   const int lim_g = g.G < g.C ? g.G : g.C;
   const int nspec = g.R + 1 + (any_empty ? lim_g + 1 : 0);
   auto spec_at = [&](int i) -> int {
     if (i < g.R) return (int)(g.pmax[bg * g.R + i] & 0xFFFFFu);
-    if (i == g.R) return g.causal ? n : -1;
+    if (i == g.R) return g.causal ? na : -1;
     i -= g.R + 1;
     if (i < lim_g) return g.glob[i];
     return g.G < g.C ? 0 : -1;
@@ -237,14 +240,14 @@ __device__ inline void finish_row(const GraphDev& g, int mode, RowHeap<KT>& heap
   for (int i = 0; i < nspec; ++i) {
     const int x = spec_at(i);
     if (x < 0 || x >= g.M) continue;  // not a key of this sequence (e.g. self when N > M)
-    if (i < g.R && g.causal && x > n) continue;  // a future pad key never appears as itself
+    if (i < g.R && g.causal && x > na) continue;  // a future pad key never appears as itself
     bool dup = false;
     for (int z = 0; z < i && !dup; ++z) dup = spec_at(z) == x;
     if (dup) continue;
-    if (!replay_first_valid(g, tids, rows, t, bg, n, x)) continue;
+    if (!replay_first_valid(g, tids, rows, t, bg, na, x)) continue;
     // Keys the scan may already have taken: not a pad key, not causal self.
     const bool scanned = !((__ldg(g.pmask + (int64_t)bg * g.Wpad + (x >> 6)) >> (x & 63)) & 1ull) &&
-                         !(g.causal && x >= n);
+                         !(g.causal && x >= na);
     if (scanned) {
       bool present = false;
       for (int z = 0; z < cnt && !present; ++z) present = heap.key(z) == x;
@@ -287,7 +290,7 @@ __device__ inline void finish_row(const GraphDev& g, int mode, RowHeap<KT>& heap
   uint8_t* vo = g.valid + ((int64_t)bh * g.N + n) * g.Wout;
   int slot = 0;
   if (!g.is_cross) {
-    nbo[0] = min(n, g.M - 1);  // merge's final clamp to the true maximum index
+    nbo[0] = min(na, g.M - 1);  // merge's final clamp to the true maximum index
     vo[0] = 1;
     slot = 1;
   }
@@ -302,7 +305,7 @@ __device__ inline void finish_row(const GraphDev& g, int mode, RowHeap<KT>& heap
     int vw = BIG;
     if (iw < kw) {
       const int o = iw - g.window;
-      int idx = (g.causal && o > 0) ? n : n + o;
+      int idx = (g.causal && o > 0) ? na : na + o;
       idx = idx < 0 ? 0 : (idx > g.M - 1 ? g.M - 1 : idx);
       vw = idx;
     }
@@ -314,7 +317,7 @@ __device__ inline void finish_row(const GraphDev& g, int mode, RowHeap<KT>& heap
     else if (v == vw) ++iw;
     else if (v == vg) ++ig;
     else zero_pending = false;
-    if (v == last || (!g.is_cross && v == n)) continue;
+    if (v == last || (!g.is_cross && v == na)) continue;
     last = v;
     nbo[slot] = v;
     vo[slot] = 1;

@@ -285,7 +285,8 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g, int stage, int mode
   const int64_t total = (int64_t)g.B * g.H * g.N;
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; row < total; row += nwarps) {
-    const int n = (int)(row % g.N);
+    const int n = (int)(row % g.N);  // row within q and the outputs
+    const int na = g.row0 + n;        // its sequence position (causal limit, window, self)
     const int64_t bh = row / g.N;
     const int b = (int)(bh / g.H), h = (int)(bh % g.H);
     const int gk = h / g.rep;
@@ -297,7 +298,7 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g, int stage, int mode
     const unsigned long long* bo = g.buf + row * g.capg;
     if (stage == 0) {
       // ---- THRESH: tau = x-th largest sampled score ----------------------
-      const int tiles_row = g.causal ? (n + 127) / 128 : (g.M + 127) / 128;
+      const int tiles_row = g.causal ? (na + 127) / 128 : (g.M + 127) / 128;
       const int sampled = tiles_row > 0 ? (tiles_row + g.sample_s - 1) / g.sample_s : 0;
       float tau = -INFINITY;
       if (sampled > 0 && tiles_row > 0) {
@@ -342,9 +343,9 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g, int stage, int mode
     int xs = -1;
     if (lane < g.R) {
       xs = (int)(g.pmax[bg * g.R + lane] & 0xFFFFFu);
-      if (g.causal && xs > n) xs = -1;  // a future pad key never appears as itself
+      if (g.causal && xs > na) xs = -1;  // a future pad key never appears as itself
     } else if (lane == g.R) {
-      xs = g.causal ? n : -1;
+      xs = g.causal ? na : -1;
     } else if (lane < ncand - 1) {
       xs = g.glob[lane - g.R - 1];
     } else if (lane == ncand - 1 && any_empty) {
@@ -384,13 +385,13 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g, int stage, int mode
         f = in ? 3 : 0;
       } else {
         bool real;
-        if (g.causal && x > n) real = false;
-        else if (g.causal && x == n) real = lc > n || member;
+        if (g.causal && x > na) real = false;
+        else if (g.causal && x == na) real = lc > na || member;
         else real = member;
         if (real) f = 1;
         else if (sz < g.C) {
           int P = (int)(pm & 0xFFFFFu);
-          if (g.causal && P > n) P = n;
+          if (g.causal && P > na) P = na;
           if (P == x) f = 2;
         }
       }
@@ -425,7 +426,7 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g, int stage, int mode
       }
       if (elig) {
         const bool scanned =
-            !((__ldg(g.pmask + (int64_t)bg * g.Wpad + (x >> 6)) >> (x & 63)) & 1ull) && !(g.causal && x >= n);
+            !((__ldg(g.pmask + (int64_t)bg * g.Wpad + (x >> 6)) >> (x & 63)) & 1ull) && !(g.causal && x >= na);
         bool present = false;
         if (scanned)
           for (int z = 0; z < c && !present; ++z) present = (int)S.ky[z] == x;
@@ -560,16 +561,16 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g, int stage, int mode
     // bitmap; the window's keys then take consecutive slots after the
     // bitmap keys below wlo.
     const bool add_zero = max(n_elig, g.G) < g.A;
-    const bool drop_self = !g.is_cross && n < g.M;
+    const bool drop_self = !g.is_cross && na < g.M;
     int wlo = 1, whi = 0, nwin = 0;
     if (!g.is_cross) {
-      wlo = min(max(n - g.window, 0), g.M - 1);
-      whi = min(max(g.causal ? n : n + g.window, 0), g.M - 1);
-      nwin = whi - wlo + 1 - ((drop_self && n >= wlo && n <= whi) ? 1 : 0);
+      wlo = min(max(na - g.window, 0), g.M - 1);
+      whi = min(max(g.causal ? na : na + g.window, 0), g.M - 1);
+      nwin = whi - wlo + 1 - ((drop_self && na >= wlo && na <= whi) ? 1 : 0);
     }
     auto mark = [&](int x) {
       if (x >= wlo && x <= whi) return;  // window key (or self inside it)
-      if (drop_self && x == n) return;
+      if (drop_self && x == na) return;
       const uint32_t old = atomicOr(&S.bits[x >> 5], 1u << (x & 31));
       if (old == 0u) atomicOr(&S.l1[x >> 10], 1u << ((x >> 5) & 31));
     };
@@ -637,11 +638,11 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g, int stage, int mode
     __syncwarp();
     for (int j = lane; j < nwin; j += 32) {
       int x = wlo + j;
-      if (drop_self && x >= n) ++x;  // skip self
+      if (drop_self && x >= na) ++x;  // skip self
       const int slot = s0 + nbelow + j;
       if (slot < g.Wout) stage_out[slot] = x;
     }
-    if (s0 == 1 && lane == 0) stage_out[0] = min(n, g.M - 1);
+    if (s0 == 1 && lane == 0) stage_out[0] = min(na, g.M - 1);
     __syncwarp();
     const int total = min(s0 + nlg + nwin, g.Wout);
     int32_t* nbo = g.nb + row * g.Wout;

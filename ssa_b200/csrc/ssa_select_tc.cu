@@ -284,7 +284,8 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
   const int bg = b * g.n_kv + gk;
   const int n0 = blockIdx.x * ROWS;
   const int n_hi = min(g.N, n0 + ROWS) - 1;
-  const int nkt_all = g.causal ? min((g.M + NKEY - 1) / NKEY, (n_hi >> 7) + 1) : (g.M + NKEY - 1) / NKEY;
+  const int nkt_all =
+      g.causal ? min((g.M + NKEY - 1) / NKEY, ((g.row0 + n_hi) >> 7) + 1) : (g.M + NKEY - 1) / NKEY;
   const int step = pass == 0 ? g.sample_s : 1;
   const int ntl = (nkt_all + step - 1) / step;  // tiles this CTA visits: 0, step, 2*step, ...
 
@@ -418,7 +419,7 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
           unsigned long long x = w[hw];
           x &= ~__ldg(g.pmask + (int64_t)bg * g.Wpad + 2 * kt + hw);
           if (g.causal) {
-            const int lim = n - (key0 + 64 * hw);
+            const int lim = g.row0 + n - (key0 + 64 * hw);  // keys before the row's position
             if (lim <= 0) x = 0ull;
             else if (lim < 64) x &= (1ull << lim) - 1ull;
           }

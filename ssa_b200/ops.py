@@ -64,7 +64,7 @@ def _stream(dev: torch.device):
     return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
 
 
-def graph_params(q, k, *, R, max_p, p_eff, C, T, A, causal, is_cross, K, window, G):
+def graph_params(q, k, *, R, max_p, p_eff, C, T, A, causal, is_cross, K, window, G, q_row0=0):
     B, H, N, d = q.shape
     Bk, n_kv, M, dk = k.shape
     if Bk != B or dk != d:
@@ -76,6 +76,7 @@ def graph_params(q, k, *, R, max_p, p_eff, C, T, A, causal, is_cross, K, window,
     p.dtype = _dtype_code(q)
     p.R, p.max_p, p.p_eff, p.C, p.T, p.A = R, max_p, p_eff, C, T, A
     p.causal, p.is_cross, p.K, p.window, p.G = int(causal), int(is_cross), K, window, G
+    p.q_row0 = int(q_row0)
     return p
 
 
@@ -92,13 +93,15 @@ def _graph_inputs(q, k, rand_proj, glob):
 
 def build_graph(q: torch.Tensor, k: torch.Tensor, rand_proj: torch.Tensor, glob: torch.Tensor, *,
                 R: int, max_p: int, p_eff: int, C: int, T: int, A: int, causal: bool,
-                is_cross: bool, K: int, window: int, want_lsh: bool = False):
+                is_cross: bool, K: int, window: int, want_lsh: bool = False, q_row0: int = 0):
     """SparseAttention.build_graph on the GPU. Returns int32 neighbors
-    (B,H,N,W), uint8 valid (B,H,N,W) and, if asked, the int32 LSH set."""
+    (B,H,N,W), uint8 valid (B,H,N,W) and, if asked, the int32 LSH set.
+    q_row0: sequence position of q's first row when q holds a slice of the
+    query rows (query-row sharding); k always holds every key."""
     q, qs, k, ks, rp, g = _graph_inputs(q, k, rand_proj, glob)
     G = g.numel() if g is not None else 0
     p = graph_params(q, k, R=R, max_p=max_p, p_eff=p_eff, C=C, T=T, A=A, causal=causal,
-                     is_cross=is_cross, K=K, window=window, G=G)
+                     is_cross=is_cross, K=K, window=window, G=G, q_row0=q_row0)
     p.q_sb, p.q_sh, p.q_sn = qs
     p.k_sb, p.k_sh, p.k_sm = ks
     L = _lib.load()
