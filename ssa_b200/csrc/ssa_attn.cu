@@ -164,6 +164,146 @@ __global__ void __launch_bounds__(256) k_attn_fwd(AttnDev a) {
 }
 
 // ---------------------------------------------------------------------------
+// Forward, vectorised: used when every row slice is 16-byte aligned and the
+// head dim is exactly 8 * EPL. The row's slot keys (-1 for slots that take
+// no part) are staged in shared memory first, so no gather waits on an index
+// load; each lane moves its 32-byte (bf16) or 64-byte (fp32) slice with
+// 16-byte loads, and every 8-lane group keeps U rows in flight.
+// ---------------------------------------------------------------------------
+template <int DT, int EPL>
+struct RawSlice {
+  static constexpr int NW = (DT == kDtF32 ? EPL * 4 : EPL * 2) / 16;  // 16-byte words
+  uint4 w[NW];
+};
+
+template <int DT, int EPL>
+__device__ __forceinline__ void raw_load(const void* row, int e0, RawSlice<DT, EPL>& r) {
+  const uint4* p = reinterpret_cast<const uint4*>(static_cast<const char*>(row) +
+                                                  (size_t)e0 * (DT == kDtF32 ? 4 : 2));
+#pragma unroll
+  for (int k = 0; k < RawSlice<DT, EPL>::NW; ++k) r.w[k] = __ldg(p + k);
+}
+
+template <int DT, int EPL>
+__device__ __forceinline__ void raw_zero(RawSlice<DT, EPL>& r) {
+#pragma unroll
+  for (int k = 0; k < RawSlice<DT, EPL>::NW; ++k) r.w[k] = make_uint4(0u, 0u, 0u, 0u);
+}
+
+// Element c of a raw slice as fp32.
+template <int DT, int EPL>
+__device__ __forceinline__ float raw_at(const RawSlice<DT, EPL>& r, int c) {
+  if constexpr (DT == kDtF32) {
+    const uint4 w = r.w[c >> 2];
+    const uint32_t u = (c & 3) == 0 ? w.x : (c & 3) == 1 ? w.y : (c & 3) == 2 ? w.z : w.w;
+    return __uint_as_float(u);
+  } else {
+    const uint4 w = r.w[c >> 3];
+    const int q = (c >> 1) & 3;
+    const uint32_t u = q == 0 ? w.x : q == 1 ? w.y : q == 2 ? w.z : w.w;
+    return __uint_as_float((c & 1) ? (u & 0xffff0000u) : (u << 16));
+  }
+}
+
+template <int DT, int EPL, bool FP32W, typename IT>
+__global__ void __launch_bounds__(256, 4) k_attn_fwd_v16(AttnDev a) {
+  constexpr int U = 4;  // rows in flight per 8-lane group
+  extern __shared__ __align__(16) float s_all[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t i = (int64_t)blockIdx.x * 8 + warp;
+  if (i >= (int64_t)a.B * a.H * a.N) return;
+  int b, h, n, g;
+  decode_row(a, i, b, h, n, g);
+  const int Kp = (a.Kn + 31) & ~31;
+  float* s = s_all + warp * 2 * Kp;
+  int* sk = reinterpret_cast<int*>(s + Kp);
+  const int grp = lane >> 3, li = lane & 7, e0 = li * EPL;
+  const int64_t row = ((int64_t)b * a.H + h) * a.N + n;
+  const void* nbr = static_cast<const char*>(a.nb) + row * a.Kn * (int64_t)sizeof(IT);
+  const uint8_t* vr = a.valid + row * a.Kn;
+  const void* kb = row_ptr<DT>(a.k, b * a.k_sb + g * a.k_sh);
+  const void* vb = row_ptr<DT>(a.v, b * a.v_sb + g * a.v_sh);
+
+  for (int j = lane; j < a.Kn; j += 32) sk[j] = slot_ok<IT>(a, nbr, vr, j) ? load_nb<IT>(nbr, j) : -1;
+  RawSlice<DT, EPL> qr;
+  raw_load<DT, EPL>(row_ptr<DT>(a.q, b * a.q_sb + h * a.q_sh + (int64_t)n * a.q_sn), e0, qr);
+  float qv[EPL];
+#pragma unroll
+  for (int c = 0; c < EPL; ++c) qv[c] = raw_at<DT, EPL>(qr, c);
+  __syncwarp();
+
+  // Pass 1: scores.
+  for (int j0 = 0; j0 < a.Kn; j0 += 4 * U) {
+    RawSlice<DT, EPL> kr[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = j0 + u * 4 + grp;
+      const int key = j < a.Kn ? sk[j] : -1;
+      if (key >= 0) raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), e0, kr[u]);
+      else raw_zero<DT, EPL>(kr[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float x = 0.f;
+#pragma unroll
+      for (int c = 0; c < EPL; ++c) x = fmaf(qv[c], raw_at<DT, EPL>(kr[u], c), x);
+      x += __shfl_xor_sync(0xffffffffu, x, 1);
+      x += __shfl_xor_sync(0xffffffffu, x, 2);
+      x += __shfl_xor_sync(0xffffffffu, x, 4);
+      const int j = j0 + u * 4 + grp;
+      if (li == 0 && j < a.Kn) s[j] = sk[j] >= 0 ? x * a.scale : -INFINITY;
+    }
+  }
+  __syncwarp();
+  // Softmax in fp32 (:1167).
+  float mx = -INFINITY;
+  for (int j = lane; j < a.Kn; j += 32) mx = fmaxf(mx, s[j]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.f;
+  for (int j = lane; j < a.Kn; j += 32) sum += expf(s[j] - mx);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  for (int j = lane; j < a.Kn; j += 32) {
+    float p = expf(s[j] - mx) / sum;
+    if (DT == kDtBF16 && !FP32W) p = round_bf16(p);  // attn.to(v.dtype) (:1190)
+    s[j] = p;
+  }
+  __syncwarp();
+  // Pass 2: weighted sum of value rows.
+  float acc[EPL];
+#pragma unroll
+  for (int c = 0; c < EPL; ++c) acc[c] = 0.f;
+  for (int j0 = 0; j0 < a.Kn; j0 += 4 * U) {
+    RawSlice<DT, EPL> vrw[U];
+    float p[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = j0 + u * 4 + grp;
+      const int key = j < a.Kn ? sk[j] : -1;
+      p[u] = key >= 0 ? s[j] : 0.f;
+      if (key >= 0) raw_load<DT, EPL>(row_ptr<DT>(vb, (int64_t)key * a.v_sm), e0, vrw[u]);
+      else raw_zero<DT, EPL>(vrw[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int c = 0; c < EPL; ++c) acc[c] = fmaf(p[u], raw_at<DT, EPL>(vrw[u], c), acc[c]);
+  }
+#pragma unroll
+  for (int c = 0; c < EPL; ++c) {
+    acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], 8);
+    acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], 16);
+  }
+  if (grp == 0) {
+    void* orow = row_ptr_mut<DT>(a.out, b * a.o_sb + h * a.o_sh + (int64_t)n * a.o_sn);
+#pragma unroll
+    for (int c = 0; c < EPL; ++c) store1<DT>(orow, e0 + c, acc[c]);
+  }
+  if (a.lse && lane == 0) a.lse[row] = mx + logf(sum);
+}
+
+// ---------------------------------------------------------------------------
 // Backward, stage 1: per row -- dq, edge weights, edge keys.
 // ---------------------------------------------------------------------------
 template <int DT, int EPL, bool FP32W, typename IT>
@@ -316,9 +456,33 @@ __global__ void __launch_bounds__(256) k_dkdv(AttnDev a, int64_t n_edges) {
 // ---------------------------------------------------------------------------
 // Host launchers
 // ---------------------------------------------------------------------------
+// The vectorised kernel needs the head dim to be exactly 8 * EPL and every
+// row slice it loads (q, k, v) to start on a 16-byte boundary.
+template <int DT, int EPL>
+static bool fwd_vec16_ok(const AttnDev& a) {
+  if (a.d != 8 * EPL) return false;
+  const int es = DT == kDtF32 ? 4 : 2;
+  auto al = [&](const void* p) { return (reinterpret_cast<uintptr_t>(p) % 16) == 0; };
+  auto st = [&](int64_t x) { return (x * es) % 16 == 0; };
+  return al(a.q) && al(a.k) && al(a.v) && st(a.q_sb) && st(a.q_sh) && st(a.q_sn) && st(a.k_sb) &&
+         st(a.k_sh) && st(a.k_sm) && st(a.v_sb) && st(a.v_sh) && st(a.v_sm);
+}
+
 template <int DT, int EPL, bool FP32W, typename IT>
 static cudaError_t fwd_t(const AttnDev& a, cudaStream_t st) {
   const int Kp = (a.Kn + 31) & ~31;
+  if constexpr (!(DT == kDtBF16 && EPL < 8)) {  // bf16 slices under 16 bytes: scalar kernel only
+    if (fwd_vec16_ok<DT, EPL>(a)) {
+      const size_t smem = (size_t)8 * 2 * Kp * sizeof(float);
+      auto fn = k_attn_fwd_v16<DT, EPL, FP32W, IT>;
+      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      const int64_t rows = (int64_t)a.B * a.H * a.N;
+      fn<<<(unsigned)((rows + 7) / 8), 256, smem, st>>>(a);
+      note_launch();
+      return cudaGetLastError();
+    }
+  }
   const size_t smem = (size_t)8 * Kp * sizeof(float);
   auto fn = k_attn_fwd<DT, EPL, FP32W, IT>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
