@@ -60,15 +60,76 @@ __global__ void __launch_bounds__(128) k_hash_queries(GraphDev g) {
 // The kth largest 16-bit order key among the candidates of a row's sample:
 // ntiles records of kSampleTileBytes (128 upper score halves, then the 128-bit
 // candidate mask). 2-pass, 8-bit radix select; lane L reads scores 4L..4L+3
-// of each record. Warp-collective.
-__device__ uint32_t warp_sample_kth(const unsigned char* base, int ntiles, int kth, uint32_t* hist) {
+// of each record. The first pass reads the records and keeps each lane's
+// candidate keys (up to kThreshCache of them) in `cache` ([kThreshCache][32]),
+// so the second pass reads shared memory, not the records again.
+constexpr int kThreshCache = 32;
+
+__device__ __forceinline__ void hist_find(uint32_t* hist, int need, int* bin_out, int* before_out) {
   const int lane = threadIdx.x & 31;
-  uint32_t prefix = 0, pmask = 0;
-  int need = kth;
-  for (int shift = 8; shift >= 0; shift -= 8) {
+  uint32_t c[8];
+  uint32_t tot = 0;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0;
-    __syncwarp();
+  for (int j = 0; j < 8; ++j) {
+    c[j] = hist[255 - (lane * 8 + j)];
+    tot += c[j];
+  }
+  uint32_t incl = tot;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  uint32_t before = incl - tot;
+  int found_bin = -1;
+  uint32_t found_before = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (found_bin < 0 && before < (uint32_t)need && before + c[j] >= (uint32_t)need) {
+      found_bin = 255 - (lane * 8 + j);
+      found_before = before;
+    }
+    before += c[j];
+  }
+  const unsigned who = __ballot_sync(0xffffffffu, found_bin >= 0);
+  const int src_lane = __ffs(who) - 1;  // exists: the histogram holds at least `need` entries
+  *bin_out = __shfl_sync(0xffffffffu, found_bin, src_lane);
+  *before_out = (int)__shfl_sync(0xffffffffu, found_before, src_lane);
+}
+
+__device__ uint32_t warp_sample_kth(const unsigned char* base, int ntiles, int kth, uint32_t* hist,
+                                    uint16_t* cache) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0;
+  __syncwarp();
+  int k = 0;  // this lane's candidates
+  for (int jt = 0; jt < ntiles; ++jt) {
+    const unsigned char* tb = base + (size_t)jt * kSampleTileBytes;
+    const uint2 kv = *reinterpret_cast<const uint2*>(tb + 8 * lane);
+    const uint32_t mw = *reinterpret_cast<const uint32_t*>(tb + 256 + 4 * (lane >> 3));
+    const uint32_t m4 = (mw >> ((4 * lane) & 31)) & 0xFu;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if ((m4 >> q) & 1u) {
+        const uint32_t h = ((q < 2 ? kv.x : kv.y) >> (16 * (q & 1))) & 0xFFFFu;
+        const uint32_t u = (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);  // okey of the upper half
+        atomicAdd(&hist[u >> 8], 1u);
+        if (k < kThreshCache) cache[k * 32 + lane] = (uint16_t)u;
+        ++k;
+      }
+    }
+  }
+  __syncwarp();
+  int hi_bin, before;
+  hist_find(hist, kth, &hi_bin, &before);
+  const int need = kth - before;
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0;
+  __syncwarp();
+  if (__any_sync(0xffffffffu, k > kThreshCache)) {
+    // some lane's candidates overflowed the cache: read the records again
     for (int jt = 0; jt < ntiles; ++jt) {
       const unsigned char* tb = base + (size_t)jt * kSampleTileBytes;
       const uint2 kv = *reinterpret_cast<const uint2*>(tb + 8 * lane);
@@ -77,45 +138,21 @@ __device__ uint32_t warp_sample_kth(const unsigned char* base, int ntiles, int k
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const uint32_t h = ((q < 2 ? kv.x : kv.y) >> (16 * (q & 1))) & 0xFFFFu;
-        const uint32_t u = (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);  // okey of the upper half
-        if (((m4 >> q) & 1u) && (u & pmask) == prefix) atomicAdd(&hist[(u >> shift) & 255u], 1u);
+        const uint32_t u = (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);
+        if (((m4 >> q) & 1u) && (int)(u >> 8) == hi_bin) atomicAdd(&hist[u & 255u], 1u);
       }
     }
-    __syncwarp();
-    uint32_t c[8];
-    uint32_t tot = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      c[j] = hist[255 - (lane * 8 + j)];
-      tot += c[j];
+  } else {
+    for (int t = 0; t < k; ++t) {
+      const uint32_t u = cache[t * 32 + lane];
+      if ((int)(u >> 8) == hi_bin) atomicAdd(&hist[u & 255u], 1u);
     }
-    uint32_t incl = tot;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    uint32_t before = incl - tot;
-    int found_bin = -1;
-    uint32_t found_before = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (found_bin < 0 && before < (uint32_t)need && before + c[j] >= (uint32_t)need) {
-        found_bin = 255 - (lane * 8 + j);
-        found_before = before;
-      }
-      before += c[j];
-    }
-    const unsigned who = __ballot_sync(0xffffffffu, found_bin >= 0);
-    const int src_lane = __ffs(who) - 1;  // exists: the sample holds at least kth candidates
-    const int bin = __shfl_sync(0xffffffffu, found_bin, src_lane);
-    const uint32_t fb = __shfl_sync(0xffffffffu, found_before, src_lane);
-    need -= (int)fb;
-    prefix |= (uint32_t)bin << shift;
-    pmask |= 0xFFu << shift;
-    __syncwarp();
   }
-  return prefix;
+  __syncwarp();
+  int lo_bin, before2;
+  hist_find(hist, need, &lo_bin, &before2);
+  __syncwarp();
+  return ((uint32_t)hi_bin << 8) | (uint32_t)lo_bin;
 }
 
 // Descending bitonic sort of one value per lane.
@@ -244,7 +281,7 @@ struct RowsSmem {
 
 // Shared-memory bytes per warp of k_rows: THRESH needs only the histogram.
 __host__ __device__ inline size_t rows_warp_bytes(const GraphDev& g, int stage) {
-  if (stage == 0) return 256 * 4;
+  if (stage == 0) return 256 * 4 + kThreshCache * 32 * 2;
   const int cap = g.capg + 64;
   const int scn = cap > g.Wout ? cap : g.Wout;
   const int Mw = (g.M + 31) / 32;
@@ -267,8 +304,10 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g, int stage, int mode
   const int nl1 = (Mw + 31) / 32;
   unsigned char* base = smem + warp * rows_warp_bytes(g, stage);
   RowsSmem S;
+  uint16_t* tcache = nullptr;
   if (stage == 0) {
     S.hist = reinterpret_cast<uint32_t*>(base);
+    tcache = reinterpret_cast<uint16_t*>(S.hist + 256);
   } else {
     S.sc = reinterpret_cast<float*>(base);
     S.ky = reinterpret_cast<uint16_t*>(S.sc + scn);
@@ -311,7 +350,8 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g, int stage, int mode
         // least x sampled scores are >= tau.
         const int fit = (int)((size_t)g.capg * 8 / kSampleTileBytes);
         if (x >= 1 && cnt_all >= x && sampled <= fit)
-          tau = okey_inv(warp_sample_kth(reinterpret_cast<const unsigned char*>(bo), sampled, x, S.hist) << 16);
+          tau = okey_inv(warp_sample_kth(reinterpret_cast<const unsigned char*>(bo), sampled, x, S.hist, tcache)
+                         << 16);
       }
       if (lane == 0) g.tau[row] = tau;
       __syncwarp();
