@@ -142,6 +142,17 @@ typedef struct {
   int64_t k_sb, k_sh, k_sm; /* (B,n_kv,M,d) */
   int64_t v_sb, v_sh, v_sm; /* (B,n_kv,M,d) */
   int64_t o_sb, o_sh, o_sn; /* out / dO / dq (B,H,N,d) */
+  /* Attention-weight dropout (F.dropout after the weights' cast,
+   * sparse_attention.py:1193-1194): each weight is zeroed with probability
+   * dropout_p, the kept ones scaled by 1 / (1 - dropout_p). 0 disables it.
+   * The keep decision of slot j of row r (row = (b*H + h)*N + n) comes from
+   * Philox4x32-10 keyed by dropout_seed, counter (e / 4, e >> 34,
+   * dropout_offset), e = r * Kn + j, output word e % 4: kept iff that word is
+   * >= dropout_p * 2^32. Forward and backward must get the same values. */
+  float dropout_p;
+  int32_t reserved0;
+  uint64_t dropout_seed;
+  uint64_t dropout_offset;
 } ssa_attn_params;
 
 /*

@@ -39,7 +39,9 @@ class AttnParams(ctypes.Structure):
                                     "fp32_weights")] + \
                [("scale", ctypes.c_float)] + \
                [(n, _i64) for n in ("q_sb", "q_sh", "q_sn", "k_sb", "k_sh", "k_sm",
-                                    "v_sb", "v_sh", "v_sm", "o_sb", "o_sh", "o_sn")]
+                                    "v_sb", "v_sh", "v_sm", "o_sb", "o_sh", "o_sn")] + \
+               [("dropout_p", ctypes.c_float), ("reserved0", _i32),
+                ("dropout_seed", ctypes.c_uint64), ("dropout_offset", ctypes.c_uint64)]
 
 
 # name -> (restype, argtypes): exactly the declarations of include/ssa_b200.h

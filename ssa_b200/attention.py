@@ -238,10 +238,11 @@ def sparse_gather_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     (B, H, M, d) or unexpanded (B, n_kv, M, d)."""
     if valid is None:
         valid = torch.ones(neighbors.shape, dtype=torch.bool, device=neighbors.device)
-    if dropout > 0.0 and training:
-        raise NotImplementedError(
-            "attention-weight dropout in training mode is not available on the B200 path yet")
-    return ops.gather_attention(q, k, v, neighbors, valid, scale, fp32_attn_weights)
+    # F.dropout on the attention weights after their cast (:1193-1194): the
+    # keep mask comes from an in-kernel counter-based generator keyed by a
+    # seed drawn here, and the backward recomputes the same mask.
+    drop = ops.new_dropout_key(dropout) if (dropout > 0.0 and training) else None
+    return ops.gather_attention(q, k, v, neighbors, valid, scale, fp32_attn_weights, dropout=drop)
 
 
 # ---------------------------------------------------------------------------
@@ -365,10 +366,9 @@ class SparseAttention(nn.Module):
         k = self._split_kv_grouped(self.Wk(src))
         v = self._split_kv_grouped(self.Wv(src))
         nb, valid = self._graph(q, k, M, causal, is_cross)
-        if self.dp > 0.0 and self.training:
-            raise NotImplementedError(
-                "attention-weight dropout in training mode is not available on the B200 path yet")
-        out = ops.gather_attention(q, k, v, nb, valid, self.scale, self.config.fp32_attn_weights)
+        drop = ops.new_dropout_key(self.dp) if (self.dp > 0.0 and self.training) else None
+        out = ops.gather_attention(q, k, v, nb, valid, self.scale, self.config.fp32_attn_weights,
+                                   dropout=drop)
         out_proj = self.Wo(out.transpose(1, 2).reshape(B, N, self.H * self.d_head))
         if not return_stats:
             return out_proj, {}
@@ -491,10 +491,9 @@ class CachedGraphSparseTransformer(nn.Module):
                 cached = self.shared_attn_per_group[group]._graph(q, k, N, attn.config.causal, False)
                 cached_group = group
             nb, valid = cached
-            if attn.dp > 0.0 and attn.training:
-                raise NotImplementedError(
-                    "attention-weight dropout in training mode is not available on the B200 path yet")
-            out = ops.gather_attention(q, k, v, nb, valid, attn.scale, attn.config.fp32_attn_weights)
+            drop = ops.new_dropout_key(attn.dp) if (attn.dp > 0.0 and attn.training) else None
+            out = ops.gather_attention(q, k, v, nb, valid, attn.scale, attn.config.fp32_attn_weights,
+                                       dropout=drop)
             a = attn.Wo(out.transpose(1, 2).reshape(B, N, attn.H * attn.d_head))
             h = h + a + layer.ff(layer.norm2(h + a))
             if return_stats:

@@ -128,6 +128,11 @@ __global__ void __launch_bounds__(256) k_attn_fwd(AttnDev a) {
   for (int j = lane; j < a.Kn; j += 32) {
     float p = expf(s[j] - mx) / sum;
     if (DT == kDtBF16 && !FP32W) p = round_bf16(p);  // attn.to(v.dtype) (:1190)
+    if (a.drop_thresh) {  // F.dropout(attn, p) (:1193-1194), in the weights' dtype
+      const bool keep = dropout_keep((unsigned long long)row * a.Kn + j, a.drop_seed, a.drop_offset,
+                                     a.drop_thresh);
+      p = keep ? ((DT == kDtBF16 && !FP32W) ? round_bf16(p * a.drop_scale) : p * a.drop_scale) : 0.f;
+    }
     s[j] = p;
   }
   __syncwarp();
@@ -267,6 +272,11 @@ __global__ void __launch_bounds__(256, 4) k_attn_fwd_v16(AttnDev a) {
   for (int j = lane; j < a.Kn; j += 32) {
     float p = expf(s[j] - mx) / sum;
     if (DT == kDtBF16 && !FP32W) p = round_bf16(p);  // attn.to(v.dtype) (:1190)
+    if (a.drop_thresh) {  // F.dropout(attn, p) (:1193-1194), in the weights' dtype
+      const bool keep = dropout_keep((unsigned long long)row * a.Kn + j, a.drop_seed, a.drop_offset,
+                                     a.drop_thresh);
+      p = keep ? ((DT == kDtBF16 && !FP32W) ? round_bf16(p * a.drop_scale) : p * a.drop_scale) : 0.f;
+    }
     s[j] = p;
   }
   __syncwarp();
@@ -356,18 +366,38 @@ __global__ void __launch_bounds__(256) k_attn_bwd_rows(AttnDev a) {
     }
   }
   __syncwarp();
+  // Dropout: the gradient reaching the pre-dropout weights is dO.v_j scaled
+  // by 1/(1-p) where the weight was kept, 0 where it was dropped. Keep bits
+  // of slots lane, lane + 32, ... stay in a register for the edge loop.
+  uint32_t keep_bits = 0xFFFFFFFFu;
+  if (a.drop_thresh) {
+    keep_bits = 0u;
+    for (int j = lane, kk = 0; j < a.Kn; j += 32, ++kk) {
+      const bool keep = dropout_keep((unsigned long long)row * a.Kn + j, a.drop_seed, a.drop_offset,
+                                     a.drop_thresh);
+      if (keep && kk < 32) keep_bits |= 1u << kk;
+      sdp[j] = keep ? sdp[j] * a.drop_scale : 0.f;
+    }
+    __syncwarp();
+  }
   float dsum = 0.f;
   for (int j = lane; j < a.Kn; j += 32) dsum = fmaf(sp[j], sdp[j], dsum);
 #pragma unroll
   for (int o = 16; o; o >>= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, o);
   const uint32_t BGM = (uint32_t)(a.B * a.n_kv) * (uint32_t)a.M;
   const uint32_t bgM = (uint32_t)(b * a.n_kv + g) * (uint32_t)a.M;
-  for (int j = lane; j < a.Kn; j += 32) {
+  for (int j = lane, kk = 0; j < a.Kn; j += 32, ++kk) {
     const float p = sp[j];
     const float ds = p * (sdp[j] - dsum) * a.scale;
     const int64_t e = row * a.Kn + j;
     const bool ok = slot_ok<IT>(a, nbr, vr, j);
-    a.ep[e] = (DT == kDtBF16 && !FP32W) ? round_bf16(p) : p;
+    float pv = (DT == kDtBF16 && !FP32W) ? round_bf16(p) : p;  // the weight that multiplied v_j
+    if (a.drop_thresh) {
+      const bool keep = kk < 32 ? ((keep_bits >> kk) & 1u) != 0
+                                : dropout_keep((unsigned long long)e, a.drop_seed, a.drop_offset, a.drop_thresh);
+      pv = keep ? ((DT == kDtBF16 && !FP32W) ? round_bf16(pv * a.drop_scale) : pv * a.drop_scale) : 0.f;
+    }
+    a.ep[e] = pv;
     a.eds[e] = ds;
     a.ekey[e] = ok ? bgM + (uint32_t)load_nb<IT>(nbr, j) : BGM;
     a.eid[e] = (uint32_t)e;

@@ -128,7 +128,7 @@ extern "C" {
 
 const char* ssa_last_error(void) { return g_err; }
 
-int32_t ssa_abi_version(void) { return 102; }
+int32_t ssa_abi_version(void) { return 103; }
 
 int32_t ssa_device_error(int32_t clear) { return ssa::read_device_error(clear); }
 
@@ -216,6 +216,8 @@ int ssa_hash_ids(const void* x, int32_t dtype, int32_t B, int32_t heads, int32_t
 
 static int check_attn(const ssa_attn_params* p, const void* q, const void* k, const void* v,
                       const void* nb, const uint8_t* valid) {
+  if (p && !(p->dropout_p >= 0.f && p->dropout_p < 1.f))
+    return fail(SSA_ERR_INVALID, "dropout_p=%g must be in [0, 1)", (double)p->dropout_p);
   int rc;
   if (!p) return fail(SSA_ERR_INVALID, "params is NULL");
   if (p->B < 1 || p->H < 1 || p->n_kv < 1 || p->N < 1 || p->M < 1 || p->d < 1 || p->Kn < 1)
@@ -242,6 +244,13 @@ static ssa::AttnDev attn_dev(const ssa_attn_params* p) {
   a.k_sb = p->k_sb; a.k_sh = p->k_sh; a.k_sm = p->k_sm;
   a.v_sb = p->v_sb; a.v_sh = p->v_sh; a.v_sm = p->v_sm;
   a.o_sb = p->o_sb; a.o_sh = p->o_sh; a.o_sn = p->o_sn;
+  if (p->dropout_p > 0.f) {
+    const double t = (double)p->dropout_p * 4294967296.0;
+    a.drop_thresh = t >= 4294967295.0 ? 0xFFFFFFFFu : (uint32_t)t;
+    a.drop_scale = (float)(1.0 / (1.0 - (double)p->dropout_p));
+    a.drop_seed = p->dropout_seed;
+    a.drop_offset = p->dropout_offset;
+  }
   return a;
 }
 

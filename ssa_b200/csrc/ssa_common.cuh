@@ -26,6 +26,34 @@ __device__ __forceinline__ float round_bf16(float f) {
   return bf16_bits_to_f32(f32_to_bf16_bits(f));
 }
 
+// Philox4x32-10, the counter-based generator of Salmon, Moraes, Dror and
+// Shaw, "Parallel random numbers: as easy as 1, 2, 3" (SC'11): ten rounds of
+// two 32x32->64 multiplies and a Weyl-sequence key schedule.
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
+  constexpr uint32_t kM0 = 0xD2511F53u, kM1 = 0xCD9E8D57u;  // round multipliers
+  constexpr uint32_t kW0 = 0x9E3779B9u, kW1 = 0xBB67AE85u;  // key increments
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t hi0 = __umulhi(kM0, c.x), lo0 = kM0 * c.x;
+    const uint32_t hi1 = __umulhi(kM1, c.z), lo1 = kM1 * c.z;
+    c = make_uint4(hi1 ^ c.y ^ k.x, lo1, hi0 ^ c.w ^ k.y, lo0);
+    k.x += kW0;
+    k.y += kW1;
+  }
+  return c;
+}
+
+// Dropout keep decision of element e (row * Kn + slot): Philox word e % 4 of
+// counter (e / 4, e >> 34, offset) under key seed, kept iff >= thresh.
+__device__ __forceinline__ bool dropout_keep(unsigned long long e, unsigned long long seed,
+                                             unsigned long long offset, uint32_t thresh) {
+  const uint4 r = philox4x32_10(make_uint4((uint32_t)(e >> 2), (uint32_t)(e >> 34), (uint32_t)offset,
+                                           (uint32_t)(offset >> 32)),
+                                make_uint2((uint32_t)seed, (uint32_t)(seed >> 32)));
+  const uint32_t w = (e & 3) == 0 ? r.x : (e & 3) == 1 ? r.y : (e & 3) == 2 ? r.z : r.w;
+  return w >= thresh;
+}
+
 // Four consecutive elements starting at element i of a row, widened to fp32.
 // The caller guarantees 16-byte (fp32) / 8-byte (bf16) alignment of row + i.
 template <int DT>

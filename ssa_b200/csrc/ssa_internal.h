@@ -88,6 +88,10 @@ cudaError_t launch_hash_ids(const void* x, int dtype, int B, int heads, int rows
 struct AttnDev {
   int B, H, n_kv, rep, N, M, d, Kn, dtype, nb_i64, fp32w;
   float scale;
+  // attention-weight dropout: drop_thresh = dropout_p * 2^32 (0: off)
+  uint32_t drop_thresh;
+  float drop_scale;   // 1 / (1 - dropout_p)
+  unsigned long long drop_seed, drop_offset;
   int64_t q_sb, q_sh, q_sn, k_sb, k_sh, k_sm, v_sb, v_sh, v_sm, o_sb, o_sh, o_sn;
   const void* q;
   const void* k;

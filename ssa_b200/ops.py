@@ -220,10 +220,27 @@ def _index_inputs(nb, valid):
     return nb, valid
 
 
+def _set_dropout(p, dropout):
+    """dropout: None, or (p, seed, offset) -- the Philox key and counter offset
+    of the keep decisions (the same triple must reach the backward)."""
+    if dropout is not None and dropout[0] > 0.0:
+        p.dropout_p = float(dropout[0])
+        p.dropout_seed = int(dropout[1]) & 0xFFFFFFFFFFFFFFFF
+        p.dropout_offset = int(dropout[2]) & 0xFFFFFFFFFFFFFFFF
+
+
+def new_dropout_key(p: float):
+    """(p, seed, offset) for one dropout application: a 62-bit seed drawn from
+    torch's default generator, so torch.manual_seed makes it reproducible and
+    every call draws a fresh mask."""
+    return (float(p), int(torch.randint(0, 2 ** 62, (1,)).item()), 0)
+
+
 def attn_fwd(q, k, v, nb, valid, scale: float, fp32w: bool, out: Optional[torch.Tensor] = None,
-             want_lse: bool = True):
+             want_lse: bool = True, dropout=None):
     """Gather attention forward. `out` (B,H,N,d) may be a strided view (for
-    example of a (B,N,H,d) buffer); returns (out, lse)."""
+    example of a (B,N,H,d) buffer); returns (out, lse). dropout: None or
+    (p, seed, offset) -- attention-weight dropout."""
     _require_cuda(q, k, v, nb, valid)
     if not (q.dtype == k.dtype == v.dtype):
         raise ValueError("q, k, v must share one dtype")
@@ -236,6 +253,7 @@ def attn_fwd(q, k, v, nb, valid, scale: float, fp32w: bool, out: Optional[torch.
         out = torch.empty((B, N, H, d), dtype=q.dtype, device=q.device).permute(0, 2, 1, 3)
     o = out.stride()
     p = _attn_params(q, k, v, nb, scale, fp32w, (o[0], o[1], o[2]))
+    _set_dropout(p, dropout)
     p.q_sb, p.q_sh, p.q_sn = qs
     p.k_sb, p.k_sh, p.k_sm = ks
     p.v_sb, p.v_sh, p.v_sm = vs
@@ -245,8 +263,9 @@ def attn_fwd(q, k, v, nb, valid, scale: float, fp32w: bool, out: Optional[torch.
     return out, lse
 
 
-def attn_bwd(q, k, v, nb, valid, dO, lse, scale: float, fp32w: bool):
-    """Gradients of sum(out * dO): dq (B,H,N,d), dk/dv (B,n_kv,M,d)."""
+def attn_bwd(q, k, v, nb, valid, dO, lse, scale: float, fp32w: bool, dropout=None):
+    """Gradients of sum(out * dO): dq (B,H,N,d), dk/dv (B,n_kv,M,d).
+    dropout: the (p, seed, offset) the forward used, or None."""
     _require_cuda(q, k, v, nb, valid, dO, lse)
     q, *qs = _rows(q)
     k, *ks = _rows(k)
@@ -258,6 +277,7 @@ def attn_bwd(q, k, v, nb, valid, dO, lse, scale: float, fp32w: bool):
     dk = torch.empty(k.shape, dtype=q.dtype, device=q.device)
     dv = torch.empty(v.shape, dtype=q.dtype, device=q.device)
     p = _attn_params(q, k, v, nb, scale, fp32w, tuple(os_))
+    _set_dropout(p, dropout)
     p.q_sb, p.q_sh, p.q_sn = qs
     p.k_sb, p.k_sh, p.k_sm = ks
     p.v_sb, p.v_sh, p.v_sm = vs
@@ -275,21 +295,22 @@ class GatherAttention(torch.autograd.Function):
     the reference (routing decisions are sign tests and top-k)."""
 
     @staticmethod
-    def forward(ctx, q, k, v, nb, valid, scale, fp32w):
-        out, lse = attn_fwd(q, k, v, nb, valid, scale, fp32w)
+    def forward(ctx, q, k, v, nb, valid, scale, fp32w, dropout=None):
+        out, lse = attn_fwd(q, k, v, nb, valid, scale, fp32w, dropout=dropout)
         ctx.save_for_backward(q, k, v, nb, valid, lse)
-        ctx.scale, ctx.fp32w = scale, fp32w
+        ctx.scale, ctx.fp32w, ctx.dropout = scale, fp32w, dropout
         ctx.mark_non_differentiable()
         return out
 
     @staticmethod
     def backward(ctx, dout):
         q, k, v, nb, valid, lse = ctx.saved_tensors
-        dq, dk, dv = attn_bwd(q, k, v, nb, valid, dout, lse, ctx.scale, ctx.fp32w)
-        return dq, dk, dv, None, None, None, None
+        dq, dk, dv = attn_bwd(q, k, v, nb, valid, dout, lse, ctx.scale, ctx.fp32w, dropout=ctx.dropout)
+        return dq, dk, dv, None, None, None, None, None
 
 
-def gather_attention(q, k, v, nb, valid, scale: float, fp32w: bool = False):
+def gather_attention(q, k, v, nb, valid, scale: float, fp32w: bool = False, dropout=None):
+    """dropout: None or (p, seed, offset); see new_dropout_key."""
     if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
-        return GatherAttention.apply(q, k, v, nb, valid, scale, fp32w)
-    return attn_fwd(q, k, v, nb, valid, scale, fp32w, want_lse=False)[0]
+        return GatherAttention.apply(q, k, v, nb, valid, scale, fp32w, dropout)
+    return attn_fwd(q, k, v, nb, valid, scale, fp32w, want_lse=False, dropout=dropout)[0]
