@@ -210,8 +210,39 @@ __device__ __forceinline__ float raw_at(const RawSlice<DT, EPL>& r, int c) {
   }
 }
 
+// Packed fp32 pairs (low element in the low word) and the sm_100 paired
+// FMA, d = a * b + c on both halves.
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+  unsigned long long d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ void f2_unpack(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b,
+                                                     unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// Elements 2*cp and 2*cp+1 of a raw slice as a packed fp32 pair.
+template <int DT, int EPL>
+__device__ __forceinline__ unsigned long long raw_pair(const RawSlice<DT, EPL>& r, int cp) {
+  if constexpr (DT == kDtF32) {
+    const uint4 w = r.w[cp >> 1];
+    return (cp & 1) ? f2_pack(__uint_as_float(w.z), __uint_as_float(w.w))
+                    : f2_pack(__uint_as_float(w.x), __uint_as_float(w.y));
+  } else {
+    const uint4 w = r.w[cp >> 2];
+    const uint32_t u = (cp & 3) == 0 ? w.x : (cp & 3) == 1 ? w.y : (cp & 3) == 2 ? w.z : w.w;
+    return f2_pack(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+  }
+}
+
 template <int DT, int EPL, bool FP32W, typename IT>
-__global__ void __launch_bounds__(256, 4) k_attn_fwd_v16(AttnDev a) {
+__global__ void __launch_bounds__(256, (EPL >= 16 ? (DT == kDtF32 ? 2 : 3) : 4)) k_attn_fwd_v16(AttnDev a) {
   constexpr int U = 4;  // rows in flight per 8-lane group
   extern __shared__ __align__(16) float s_all[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -232,9 +263,9 @@ __global__ void __launch_bounds__(256, 4) k_attn_fwd_v16(AttnDev a) {
   for (int j = lane; j < a.Kn; j += 32) sk[j] = slot_ok<IT>(a, nbr, vr, j) ? load_nb<IT>(nbr, j) : -1;
   RawSlice<DT, EPL> qr;
   raw_load<DT, EPL>(row_ptr<DT>(a.q, b * a.q_sb + h * a.q_sh + (int64_t)n * a.q_sn), e0, qr);
-  float qv[EPL];
+  unsigned long long q2[EPL / 2];
 #pragma unroll
-  for (int c = 0; c < EPL; ++c) qv[c] = raw_at<DT, EPL>(qr, c);
+  for (int c = 0; c < EPL / 2; ++c) q2[c] = raw_pair<DT, EPL>(qr, c);
   __syncwarp();
 
   // Pass 1: scores.
@@ -249,9 +280,12 @@ __global__ void __launch_bounds__(256, 4) k_attn_fwd_v16(AttnDev a) {
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      float x = 0.f;
+      unsigned long long x2 = 0ull;
 #pragma unroll
-      for (int c = 0; c < EPL; ++c) x = fmaf(qv[c], raw_at<DT, EPL>(kr[u], c), x);
+      for (int c = 0; c < EPL / 2; ++c) x2 = f2_fma(q2[c], raw_pair<DT, EPL>(kr[u], c), x2);
+      float xl, xh;
+      f2_unpack(x2, xl, xh);
+      float x = xl + xh;
       x += __shfl_xor_sync(0xffffffffu, x, 1);
       x += __shfl_xor_sync(0xffffffffu, x, 2);
       x += __shfl_xor_sync(0xffffffffu, x, 4);
@@ -281,9 +315,9 @@ __global__ void __launch_bounds__(256, 4) k_attn_fwd_v16(AttnDev a) {
   }
   __syncwarp();
   // Pass 2: weighted sum of value rows.
-  float acc[EPL];
+  unsigned long long acc2[EPL / 2];
 #pragma unroll
-  for (int c = 0; c < EPL; ++c) acc[c] = 0.f;
+  for (int c = 0; c < EPL / 2; ++c) acc2[c] = 0ull;
   for (int j0 = 0; j0 < a.Kn; j0 += 4 * U) {
     RawSlice<DT, EPL> vrw[U];
     float p[U];
@@ -296,10 +330,15 @@ __global__ void __launch_bounds__(256, 4) k_attn_fwd_v16(AttnDev a) {
       else raw_zero<DT, EPL>(vrw[u]);
     }
 #pragma unroll
-    for (int u = 0; u < U; ++u)
+    for (int u = 0; u < U; ++u) {
+      const unsigned long long pp = f2_pack(p[u], p[u]);
 #pragma unroll
-      for (int c = 0; c < EPL; ++c) acc[c] = fmaf(p[u], raw_at<DT, EPL>(vrw[u], c), acc[c]);
+      for (int c = 0; c < EPL / 2; ++c) acc2[c] = f2_fma(pp, raw_pair<DT, EPL>(vrw[u], c), acc2[c]);
+    }
   }
+  float acc[EPL];
+#pragma unroll
+  for (int c = 0; c < EPL / 2; ++c) f2_unpack(acc2[c], acc[2 * c], acc[2 * c + 1]);
 #pragma unroll
   for (int c = 0; c < EPL; ++c) {
     acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], 8);
@@ -501,7 +540,8 @@ static bool fwd_vec16_ok(const AttnDev& a) {
 template <int DT, int EPL, bool FP32W, typename IT>
 static cudaError_t fwd_t(const AttnDev& a, cudaStream_t st) {
   const int Kp = (a.Kn + 31) & ~31;
-  if constexpr (!(DT == kDtBF16 && EPL < 8)) {  // bf16 slices under 16 bytes: scalar kernel only
+  // bf16 slices under 16 bytes, and head dims above 128: scalar kernel only
+  if constexpr (!(DT == kDtBF16 && EPL < 8) && EPL <= 16) {
     if (fwd_vec16_ok<DT, EPL>(a)) {
       const size_t smem = (size_t)8 * 2 * Kp * sizeof(float);
       auto fn = k_attn_fwd_v16<DT, EPL, FP32W, IT>;
