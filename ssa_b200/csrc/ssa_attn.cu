@@ -210,23 +210,6 @@ __device__ __forceinline__ float raw_at(const RawSlice<DT, EPL>& r, int c) {
   }
 }
 
-// Packed fp32 pairs (low element in the low word) and the sm_100 paired
-// FMA, d = a * b + c on both halves.
-__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
-  unsigned long long d;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
-  return d;
-}
-__device__ __forceinline__ void f2_unpack(unsigned long long v, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b,
-                                                     unsigned long long c) {
-  unsigned long long d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-
 // Elements 2*cp and 2*cp+1 of a raw slice as a packed fp32 pair.
 template <int DT, int EPL>
 __device__ __forceinline__ unsigned long long raw_pair(const RawSlice<DT, EPL>& r, int cp) {

@@ -26,6 +26,23 @@ __device__ __forceinline__ float round_bf16(float f) {
   return bf16_bits_to_f32(f32_to_bf16_bits(f));
 }
 
+// Packed fp32 pairs (low element in the low word) and the sm_100 paired
+// FMA, d = a * b + c on both halves.
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+  unsigned long long d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ void f2_unpack(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b,
+                                                     unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
 // Philox4x32-10, the counter-based generator of Salmon, Moraes, Dror and
 // Shaw, "Parallel random numbers: as easy as 1, 2, 3" (SC'11): ten rounds of
 // two 32x32->64 multiplies and a Weyl-sequence key schedule.

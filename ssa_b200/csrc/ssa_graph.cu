@@ -72,17 +72,18 @@ __global__ void __launch_bounds__(256) k_hash_keys(GraphDev g) {
     uint32_t code = 0;
     for (int j = 0; j < g.p; ++j) {
       const float* pl = s_planes + (r * g.p + j) * g.d;
-      float s0 = 0.f, s1 = 0.f;
+      // even elements in the low half, odd ones in the high half, in order
+      unsigned long long s2 = 0ull;
 #pragma unroll
       for (int t = 0; t < D; t += 4) {
         if (t < g.d) {
           const float4 w = *reinterpret_cast<const float4*>(pl + t);
-          s0 = fmaf(x[t], w.x, s0);
-          s1 = fmaf(x[t + 1], w.y, s1);
-          s0 = fmaf(x[t + 2], w.z, s0);
-          s1 = fmaf(x[t + 3], w.w, s1);
+          s2 = f2_fma(f2_pack(x[t], x[t + 1]), f2_pack(w.x, w.y), s2);
+          s2 = f2_fma(f2_pack(x[t + 2], x[t + 3]), f2_pack(w.z, w.w), s2);
         }
       }
+      float s0, s1;
+      f2_unpack(s2, s0, s1);
       if (s0 + s1 > 0.f) code |= 1u << j;  // proj > 0, strict (:589)
     }
     g.kcode[((int64_t)bg * g.R + r) * g.M + m] = (uint16_t)code;

@@ -170,17 +170,19 @@ __device__ inline bool hash_row_ids(const GraphDev& g, const float* q, int bg, u
     uint32_t id = 0;
     for (int j = 0; j < g.p; ++j) {
       const float* pl = g.rp + ((int64_t)r * g.max_p + j) * g.d;
-      float s0 = 0.f, s1 = 0.f;
+      // Even elements accumulate into the low half, odd ones into the high
+      // half, in element order; the projection is their sum.
+      unsigned long long s2 = 0ull;
 #pragma unroll
       for (int i = 0; i < D; i += 4) {
         if (i < g.d) {
           const float4 w = __ldg(reinterpret_cast<const float4*>(pl + i));
-          s0 = fmaf(q[i], w.x, s0);
-          s1 = fmaf(q[i + 1], w.y, s1);
-          s0 = fmaf(q[i + 2], w.z, s0);
-          s1 = fmaf(q[i + 3], w.w, s1);
+          s2 = f2_fma(f2_pack(q[i], q[i + 1]), f2_pack(w.x, w.y), s2);
+          s2 = f2_fma(f2_pack(q[i + 2], q[i + 3]), f2_pack(w.z, w.w), s2);
         }
       }
+      float s0, s1;
+      f2_unpack(s2, s0, s1);
       const float s = s0 + s1;
       if (s > 0.f) id |= 1u << j;
       if (g.Te > 0) {
