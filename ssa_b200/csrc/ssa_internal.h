@@ -31,7 +31,7 @@ struct GraphDev {
   int32_t* lastc;                 // [BG][R][NB] key at rank min(size, C) - 1
   // tensor-core path (bf16): per query row
   int use_tc, capg, sample_s, fallback_only;
-  uint16_t* qids;                 // [B*H*N][NT] bucket id per (round, probe) slot
+  uint16_t* qids;                 // [NT][B*H*N] r * NB + bucket id per (round r, probe) slot
   uint8_t* qempty;                // [B*H*N] some slot's bucket is empty
   float* tau;                     // [B*H*N] scan threshold
   int32_t* rcnt;                  // [B*H*N][2] kept candidates per scan group (> capg/2: overflow)

@@ -49,7 +49,8 @@ __global__ void __launch_bounds__(128) k_hash_queries(GraphDev g) {
     }
   }
   const bool empty = hash_row_ids<D>(g, q, bg, tids, 128, t);
-  for (int tt = 0; tt < g.NT; ++tt) g.qids[row * g.NT + tt] = tids[tt * 128 + t];
+  for (int tt = 0; tt < g.NT; ++tt)
+    g.qids[(int64_t)tt * total + row] = (uint16_t)((tt / (1 + g.Te)) * g.NB + tids[tt * 128 + t]);
   g.qempty[row] = empty ? 1 : 0;
 }
 
@@ -63,7 +64,7 @@ __global__ void __launch_bounds__(128) k_hash_queries(GraphDev g) {
 // of each record. The first pass reads the records and keeps each lane's
 // candidate keys (up to kThreshCache of them) in `cache` ([kThreshCache][32]),
 // so the second pass reads shared memory, not the records again.
-constexpr int kThreshCache = 32;
+constexpr int kThreshCache = 64;
 
 __device__ __forceinline__ void hist_find(uint32_t* hist, int need, int* bin_out, int* before_out) {
   const int lane = threadIdx.x & 31;
@@ -97,62 +98,92 @@ __device__ __forceinline__ void hist_find(uint32_t* hist, int need, int* bin_out
   *before_out = (int)__shfl_sync(0xffffffffu, found_before, src_lane);
 }
 
-__device__ uint32_t warp_sample_kth(const unsigned char* base, int ntiles, int kth, uint32_t* hist,
-                                    uint16_t* cache) {
+// Reads every candidate's 16-bit order key of the sample (lane L: scores
+// 4L..4L+3 of each record) and calls f(u) for each.
+template <typename F>
+__device__ __forceinline__ void for_sample_keys(const unsigned char* base, int ntiles, F&& f) {
   const int lane = threadIdx.x & 31;
+  for (int j0 = 0; j0 < ntiles; j0 += 4) {
+    uint2 kv[4];
+    uint32_t mw[4];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0;
-  __syncwarp();
-  int k = 0;  // this lane's candidates
-  for (int jt = 0; jt < ntiles; ++jt) {
-    const unsigned char* tb = base + (size_t)jt * kSampleTileBytes;
-    const uint2 kv = *reinterpret_cast<const uint2*>(tb + 8 * lane);
-    const uint32_t mw = *reinterpret_cast<const uint32_t*>(tb + 256 + 4 * (lane >> 3));
-    const uint32_t m4 = (mw >> ((4 * lane) & 31)) & 0xFu;
+    for (int u = 0; u < 4; ++u) {  // four records' loads in flight before any use
+      const unsigned char* tb = base + (size_t)(j0 + u) * kSampleTileBytes;
+      const bool in = j0 + u < ntiles;
+      kv[u] = in ? *reinterpret_cast<const uint2*>(tb + 8 * lane) : make_uint2(0u, 0u);
+      mw[u] = in ? *reinterpret_cast<const uint32_t*>(tb + 256 + 4 * (lane >> 3)) : 0u;
+    }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      if ((m4 >> q) & 1u) {
-        const uint32_t h = ((q < 2 ? kv.x : kv.y) >> (16 * (q & 1))) & 0xFFFFu;
-        const uint32_t u = (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);  // okey of the upper half
-        atomicAdd(&hist[u >> 8], 1u);
-        if (k < kThreshCache) cache[k * 32 + lane] = (uint16_t)u;
-        ++k;
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t m4 = (mw[u] >> ((4 * lane) & 31)) & 0xFu;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if ((m4 >> q) & 1u) {
+          const uint32_t h = ((q < 2 ? kv[u].x : kv[u].y) >> (16 * (q & 1))) & 0xFFFFu;
+          f((h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u));  // okey of the upper half
+        }
       }
     }
   }
+}
+
+__device__ uint32_t warp_sample_kth(const unsigned char* base, int ntiles, int kth, uint32_t* hist,
+                                    uint16_t* cache) {
+  const int lane = threadIdx.x & 31;
+  // Pass 1 (the records): this lane's candidates into the cache, and the
+  // range [umin, umax] of all of them.
+  int k = 0;
+  uint32_t umin = 0xFFFFu, umax = 0u;
+  for_sample_keys(base, ntiles, [&](uint32_t u) {
+    if (k < kThreshCache) cache[k * 32 + lane] = (uint16_t)u;
+    ++k;
+    umin = min(umin, u);
+    umax = max(umax, u);
+  });
+  umin = __reduce_min_sync(0xffffffffu, umin);
+  umax = __reduce_max_sync(0xffffffffu, umax);
+  if (umin == umax) return umin;
+  const bool cached = !__any_sync(0xffffffffu, k > kThreshCache);
+  const int kc = min(k, kThreshCache);
+  // Pass 2: 256 bins of width 2^sh over [umin, umax] (spread over the range,
+  // so the shared-memory atomics rarely collide).
+  const uint32_t span1 = umax - umin;
+  const int bl = 32 - __clz(span1);
+  const int sh = bl > 8 ? bl - 8 : 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0;
   __syncwarp();
-  int hi_bin, before;
-  hist_find(hist, kth, &hi_bin, &before);
+  auto add_top = [&](uint32_t u) { atomicAdd(&hist[(u - umin) >> sh], 1u); };
+  if (cached) {
+    for (int t = 0; t < kc; ++t) add_top(cache[t * 32 + lane]);
+  } else {
+    for_sample_keys(base, ntiles, add_top);
+  }
+  __syncwarp();
+  int bin, before;
+  hist_find(hist, kth, &bin, &before);
+  const uint32_t lo = umin + ((uint32_t)bin << sh);
+  if (sh == 0) return lo;
+  // Pass 3: the low sh bits of the keys in that bin.
   const int need = kth - before;
   __syncwarp();
 #pragma unroll
   for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0;
   __syncwarp();
-  if (__any_sync(0xffffffffu, k > kThreshCache)) {
-    // some lane's candidates overflowed the cache: read the records again
-    for (int jt = 0; jt < ntiles; ++jt) {
-      const unsigned char* tb = base + (size_t)jt * kSampleTileBytes;
-      const uint2 kv = *reinterpret_cast<const uint2*>(tb + 8 * lane);
-      const uint32_t mw = *reinterpret_cast<const uint32_t*>(tb + 256 + 4 * (lane >> 3));
-      const uint32_t m4 = (mw >> ((4 * lane) & 31)) & 0xFu;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint32_t h = ((q < 2 ? kv.x : kv.y) >> (16 * (q & 1))) & 0xFFFFu;
-        const uint32_t u = (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);
-        if (((m4 >> q) & 1u) && (int)(u >> 8) == hi_bin) atomicAdd(&hist[u & 255u], 1u);
-      }
-    }
+  const uint32_t lmask = (1u << sh) - 1u;
+  auto add_low = [&](uint32_t u) {
+    if (((u - umin) >> sh) == (uint32_t)bin) atomicAdd(&hist[(u - umin) & lmask], 1u);
+  };
+  if (cached) {
+    for (int t = 0; t < kc; ++t) add_low(cache[t * 32 + lane]);
   } else {
-    for (int t = 0; t < k; ++t) {
-      const uint32_t u = cache[t * 32 + lane];
-      if ((int)(u >> 8) == hi_bin) atomicAdd(&hist[u & 255u], 1u);
-    }
+    for_sample_keys(base, ntiles, add_low);
   }
   __syncwarp();
-  int lo_bin, before2;
-  hist_find(hist, need, &lo_bin, &before2);
+  int bin2, before2;
+  hist_find(hist, need, &bin2, &before2);
   __syncwarp();
-  return ((uint32_t)hi_bin << 8) | (uint32_t)lo_bin;
+  return lo + (uint32_t)bin2;
 }
 
 // Descending bitonic sort of one value per lane.
@@ -398,7 +429,7 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g, int stage, int mode
     if (keep) S.spec[__popc(km & ((1u << lane) - 1u))] = xs;
     const int nspec = __popc(km);
     __syncwarp();
-    const uint16_t* tids = g.qids + row * g.NT;
+    const uint16_t* toffs = g.qids + row;  // slot tt at toffs[tt * total]: r * NB + bucket
     // Replay, lane-parallel over (key, slot) pairs: flag 1 = key's slot in
     // this (round, probe) bucket is a real member, 2 = it is the overflow pad,
     // 0 = absent (or the bucket is empty: handled as a third state 3 = present
@@ -407,9 +438,10 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g, int stage, int mode
     auto replay = [&](int p) -> uint8_t {
       const int i = p / g.NT, tt = p - i * g.NT;
       const int x = S.spec[i];
-      const int r = tt / (1 + g.Te);
-      const int u = __ldg(tids + tt);
-      const int64_t tb = (int64_t)(bg * g.R + r) * g.NB + u;
+      const int off = __ldg(toffs + (int64_t)tt * total);
+      const int r = off >> g.p;
+      const int u = off & (g.NB - 1);
+      const int64_t tb = (int64_t)bg * g.R * g.NB + off;
       const int sz = __ldg(g.bsize + tb);
       const int lc = __ldg(g.lastc + tb);
       const uint32_t pm = __ldg(g.pmax + bg * g.R + r);

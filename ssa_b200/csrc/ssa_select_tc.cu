@@ -378,7 +378,7 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
     const int64_t row = (int64_t)bh * g.N + n;
     if (act && grp == 0)
       for (int tt = 0; tt < g.NT; ++tt)
-        toff[tt * ROWS + t] = (uint16_t)((tt / (1 + g.Te)) * g.NB + g.qids[row * g.NT + tt]);
+        toff[tt * ROWS + t] = g.qids[(int64_t)tt * ((int64_t)g.B * g.H * g.N) + row];
     asm volatile("bar.sync 1, 256;" ::: "memory");  // both groups see the offsets
     const float thr = (pass == 1 && act) ? g.tau[row] : -INFINITY;
     const int half_cap = g.capg >> 1;
