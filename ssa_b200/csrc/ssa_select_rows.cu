@@ -324,9 +324,12 @@ __host__ __device__ inline size_t rows_warp_bytes(const GraphDev& g, int stage) 
 // ---------------------------------------------------------------------------
 // k_rows
 // ---------------------------------------------------------------------------
-template <int DT, int D>
-__global__ void __launch_bounds__(128, 8) k_rows(GraphDev g, int stage, int mode) {
-  // stage 0 = THRESH, 1 = FINAL
+// One instantiation per stage (0 = THRESH, 1 = FINAL) and output mode (FINAL:
+// 0 = merged neighbor rows, 1 = LSH rows in topk order), so each kernel
+// carries only its own code.
+template <int DT, int D, int STAGE, int MODE>
+__global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
+  constexpr int stage = STAGE, mode = MODE;
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cap = g.capg + 64;
@@ -761,8 +764,11 @@ cudaError_t launch_rows(const GraphDev& g, int stage, int mode, cudaStream_t st)
   constexpr int kWarps = 4;
   const size_t sm = (size_t)kWarps * rows_warp_bytes(g, stage);
   if (sm > 227 * 1024) return cudaErrorInvalidConfiguration;
-  auto fn = g.dtype == kDtF32 ? (g.d <= 64 ? k_rows<kDtF32, 64> : k_rows<kDtF32, 128>)
-                              : (g.d <= 64 ? k_rows<kDtBF16, 64> : k_rows<kDtBF16, 128>);
+  if (g.dtype != kDtBF16) return cudaErrorInvalidValue;  // the tensor-core path is bf16 only
+  auto pick = [&](auto d64, auto d128) { return g.d <= 64 ? d64 : d128; };
+  auto fn = stage == 0 ? pick(k_rows<kDtBF16, 64, 0, 0>, k_rows<kDtBF16, 128, 0, 0>)
+          : mode == 0  ? pick(k_rows<kDtBF16, 64, 1, 0>, k_rows<kDtBF16, 128, 1, 0>)
+                       : pick(k_rows<kDtBF16, 64, 1, 1>, k_rows<kDtBF16, 128, 1, 1>);
   cudaError_t e;
   if ((e = smem_attr(fn, sm)) != cudaSuccess) return e;
   int per_sm = 0;
@@ -775,7 +781,7 @@ cudaError_t launch_rows(const GraphDev& g, int stage, int mode, cudaStream_t st)
   int64_t blocks = (rows + kWarps - 1) / kWarps;
   const int64_t resident = (int64_t)nsm * per_sm;
   if (blocks > resident) blocks = resident;
-  fn<<<(unsigned)blocks, kWarps * 32, sm, st>>>(g, stage, mode);
+  fn<<<(unsigned)blocks, kWarps * 32, sm, st>>>(g);
   note_launch();
   return cudaGetLastError();
 }

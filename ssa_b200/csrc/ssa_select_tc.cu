@@ -249,11 +249,11 @@ __host__ __device__ inline SmemPlan plan(int D, const GraphDev& g) {
 // the half of the row's buffer that belongs to the tile's epilogue group.
 // rcnt[row][group] counts the candidates seen (pass 0) or kept (pass 1; above
 // half the buffer means overflow).
-template <int D>
+template <int D, int PASS>
 __global__ void __launch_bounds__(tc::THREADS, 2)
-    k_scan_tc(GraphDev g, int pass, const __grid_constant__ CUtensorMap qmap,
-              const __grid_constant__ CUtensorMap kmap) {
+    k_scan_tc(GraphDev g, const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap) {
   using namespace tc;
+  constexpr int pass = PASS;  // one instantiation per pass
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -553,11 +553,11 @@ template <int D>
 static cudaError_t launch_scan_t(const GraphDev& g, int pass, const CUtensorMap& qmap,
                                  const CUtensorMap& kmap, cudaStream_t st) {
   const tc::SmemPlan sp = tc::plan(D, g);
-  auto fn = k_scan_tc<D>;
+  auto fn = pass == 0 ? k_scan_tc<D, 0> : k_scan_tc<D, 1>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp.total);
   if (e != cudaSuccess) return e;
   dim3 grid((g.N + tc::ROWS - 1) / tc::ROWS, g.B * g.H);
-  fn<<<grid, tc::THREADS, sp.total, st>>>(g, pass, qmap, kmap);
+  fn<<<grid, tc::THREADS, sp.total, st>>>(g, qmap, kmap);
   note_launch();
   return cudaGetLastError();
 }
