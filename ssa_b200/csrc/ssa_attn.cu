@@ -27,6 +27,9 @@
 
 namespace ssa {
 
+// Sorted edges per warp in the dk / dv reduction.
+constexpr int kDkdvChunk = 512;
+
 __device__ __forceinline__ void decode_row(const AttnDev& a, int64_t i, int& b, int& h, int& n,
                                            int& g) {
   const int hh = (int)(i % a.rep);
@@ -465,43 +468,139 @@ __device__ __forceinline__ int64_t lower_bound_u32(const uint32_t* a, int64_t n,
   return lo;
 }
 
-template <int DT, int EPW>
-__global__ void __launch_bounds__(256) k_dkdv(AttnDev a, int64_t n_edges) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t key = (int64_t)blockIdx.x * 8 + warp;  // bg * M + m
+// First sorted position of every key (and of the sentinel key, the end of
+// the valid edges): one thread per key, a binary search over the sorted keys.
+__global__ void __launch_bounds__(256) k_seg_starts(AttnDev a, int64_t n_edges) {
+  const int64_t key = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t total = (int64_t)a.B * a.n_kv * a.M;
-  if (key >= total) return;
-  const int64_t lo = lower_bound_u32(a.skey, n_edges, (uint32_t)key);
-  const int64_t hi = lower_bound_u32(a.skey, n_edges, (uint32_t)key + 1u);
-  float dk[EPW], dv[EPW];
-#pragma unroll
-  for (int c = 0; c < EPW; ++c) dk[c] = dv[c] = 0.f;
-  const int e0 = lane * EPW;
-  for (int64_t s = lo; s < hi; ++s) {
-    const uint32_t e = __ldg(a.sid + s);
+  if (key > total) return;
+  a.seg[key] = (uint32_t)lower_bound_u32(a.skey, n_edges, (uint32_t)key);
+}
+
+// dk / dv as a segmented sum over the edges sorted by (kv slice, key). Each
+// warp takes a fixed chunk of kDkdvChunk sorted edges, so a key that many
+// queries gathered (a global token) is spread over many warps. Within the
+// chunk the warp walks its keys in order; a row of d elements takes d / EPW
+// lanes (rounded up to a power of two) and the warp's lane groups take
+// every G-th edge, two at a time, summed at the end in a fixed order. A key
+// whose edges all lie in the chunk is written to dk / dv; a key that crosses
+// a chunk edge leaves a partial (slot 0: it started before the chunk, slot
+// 1: it started inside), which k_dkdv_fix adds up in chunk order. The
+// result is deterministic.
+template <int DT, int EPW>
+__global__ void __launch_bounds__(256) k_dkdv(AttnDev a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t total = (int64_t)a.B * a.n_kv * a.M;
+  const int64_t ev = __ldg(a.seg + total);  // end of the valid edges
+  const int64_t chunk = (int64_t)blockIdx.x * 8 + warp;
+  const int64_t s0 = chunk * kDkdvChunk;
+  if (s0 >= ev) return;
+  const int64_t s1 = min(s0 + (int64_t)kDkdvChunk, ev);
+  int lpr = 1;  // lanes per row
+  while (lpr * EPW < a.d && lpr < 32) lpr <<= 1;
+  const int G = 32 / lpr, grp = lane / lpr, e0 = (lane % lpr) * EPW;
+  const bool in_d = e0 < a.d;
+  auto rows_of = [&](uint32_t e, const void*& qr, const void*& gr) {
     const int64_t row = e / (uint32_t)a.Kn;
     const int n = (int)(row % a.N);
     const int64_t bh = row / a.N;
     const int h = (int)(bh % a.H), b = (int)(bh / a.H);
-    const float p = __ldg(a.ep + e), ds = __ldg(a.eds + e);
-    const void* qr = row_ptr<DT>(a.q, b * a.q_sb + h * a.q_sh + (int64_t)n * a.q_sn);
-    const void* gr = row_ptr<DT>(a.dO, b * a.o_sb + h * a.o_sh + (int64_t)n * a.o_sn);
+    qr = row_ptr<DT>(a.q, b * a.q_sb + h * a.q_sh + (int64_t)n * a.q_sn);
+    gr = row_ptr<DT>(a.dO, b * a.o_sb + h * a.o_sh + (int64_t)n * a.o_sn);
+  };
+  const int64_t k_first = __ldg(a.skey + s0), k_last = __ldg(a.skey + s1 - 1);
+  for (int64_t key = k_first; key <= k_last; ++key) {
+    const int64_t kb = __ldg(a.seg + key), ke = __ldg(a.seg + key + 1);
+    const int64_t lo = max(kb, s0), hi = min(ke, s1);
+    if (lo >= hi) continue;
+    float dk[EPW], dv[EPW];
 #pragma unroll
-    for (int c = 0; c < EPW; ++c) {
-      if (e0 + c < a.d) {
-        dk[c] = fmaf(ds, load1<DT>(qr, e0 + c), dk[c]);
-        dv[c] = fmaf(p, load1<DT>(gr, e0 + c), dv[c]);
+    for (int c = 0; c < EPW; ++c) dk[c] = dv[c] = 0.f;
+    for (int64_t s = lo + grp; s < hi; s += 2 * G) {
+      const bool two = s + G < hi;
+      const uint32_t ea = __ldg(a.sid + s), eb = two ? __ldg(a.sid + s + G) : ea;
+      const void *qa, *ga, *qb, *gb;
+      rows_of(ea, qa, ga);
+      rows_of(eb, qb, gb);
+      float xq[2][EPW], xg[2][EPW];
+      if (in_d) {
+        load_slice<DT, EPW>(qa, e0, a.d, xq[0]);
+        load_slice<DT, EPW>(ga, e0, a.d, xg[0]);
+        load_slice<DT, EPW>(qb, e0, a.d, xq[1]);
+        load_slice<DT, EPW>(gb, e0, a.d, xg[1]);
+      }
+      const float pa = __ldg(a.ep + ea), da = __ldg(a.eds + ea);
+      const float pb = two ? __ldg(a.ep + eb) : 0.f, db = two ? __ldg(a.eds + eb) : 0.f;
+      if (in_d) {
+#pragma unroll
+        for (int c = 0; c < EPW; ++c) {
+          dk[c] = fmaf(da, xq[0][c], dk[c]);
+          dv[c] = fmaf(pa, xg[0][c], dv[c]);
+        }
+#pragma unroll
+        for (int c = 0; c < EPW; ++c) {
+          dk[c] = fmaf(db, xq[1][c], dk[c]);
+          dv[c] = fmaf(pb, xg[1][c], dv[c]);
+        }
+      }
+    }
+    for (int off = lpr; off < 32; off <<= 1) {
+#pragma unroll
+      for (int c = 0; c < EPW; ++c) {
+        dk[c] += __shfl_xor_sync(0xffffffffu, dk[c], off);
+        dv[c] += __shfl_xor_sync(0xffffffffu, dv[c], off);
+      }
+    }
+    if (grp == 0) {
+      if (kb >= s0 && ke <= s1) {  // the whole segment lies in this chunk
+        void* dkr = row_ptr_mut<DT>(a.dk, key * a.d);
+        void* dvr = row_ptr_mut<DT>(a.dv, key * a.d);
+#pragma unroll
+        for (int c = 0; c < EPW; ++c) {
+          if (e0 + c < a.d) {
+            store1<DT>(dkr, e0 + c, dk[c]);
+            store1<DT>(dvr, e0 + c, dv[c]);
+          }
+        }
+      } else {
+        float* pt = a.part + ((size_t)chunk * 2 + (kb < s0 ? 0 : 1)) * 2 * a.d;
+#pragma unroll
+        for (int c = 0; c < EPW; ++c) {
+          if (e0 + c < a.d) {
+            pt[e0 + c] = dk[c];
+            pt[a.d + e0 + c] = dv[c];
+          }
+        }
       }
     }
   }
+}
+
+// Keys without edges get zero gradients; keys whose edges cross a chunk
+// edge get their partials summed in chunk order. One warp per key.
+template <int DT>
+__global__ void __launch_bounds__(256) k_dkdv_fix(AttnDev a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t key = (int64_t)blockIdx.x * 8 + warp;
+  const int64_t total = (int64_t)a.B * a.n_kv * a.M;
+  if (key >= total) return;
+  const int64_t kb = __ldg(a.seg + key), ke = __ldg(a.seg + key + 1);
+  const bool empty = kb >= ke;
+  const int64_t c0 = kb / kDkdvChunk, c1 = empty ? c0 : (ke - 1) / kDkdvChunk;
+  if (!empty && c0 == c1) return;  // written by k_dkdv
   void* dkr = row_ptr_mut<DT>(a.dk, key * a.d);
   void* dvr = row_ptr_mut<DT>(a.dv, key * a.d);
-#pragma unroll
-  for (int c = 0; c < EPW; ++c) {
-    if (e0 + c < a.d) {
-      store1<DT>(dkr, e0 + c, dk[c]);
-      store1<DT>(dvr, e0 + c, dv[c]);
+  for (int e = lane; e < a.d; e += 32) {
+    float dk = 0.f, dv = 0.f;
+    if (!empty) {
+      for (int64_t c = c0; c <= c1; ++c) {
+        const float* pt = a.part + ((size_t)c * 2 + (c == c0 ? 1 : 0)) * 2 * a.d;
+        dk += __ldg(pt + e);
+        dv += __ldg(pt + a.d + e);
+      }
     }
+    store1<DT>(dkr, e, dk);
+    store1<DT>(dvr, e, dv);
   }
 }
 
@@ -577,6 +676,9 @@ size_t attn_bwd_workspace_layout(const AttnDev& a, AttnDev* out, void* ws) {
   };
   const size_t o_ep = take(4 * E), o_eds = take(4 * E), o_ekey = take(4 * E), o_eid = take(4 * E);
   const size_t o_skey = take(4 * E), o_sid = take(4 * E), o_tmp = take(tmp);
+  const size_t o_seg = take(4 * ((size_t)a.B * a.n_kv * a.M + 1));
+  const size_t chunks = (size_t)(E + kDkdvChunk - 1) / kDkdvChunk;
+  const size_t o_part = take(sizeof(float) * chunks * 4 * (size_t)a.d);
   if (out) {
     char* base = static_cast<char*>(ws);
     out->ep = reinterpret_cast<float*>(base + o_ep);
@@ -586,6 +688,8 @@ size_t attn_bwd_workspace_layout(const AttnDev& a, AttnDev* out, void* ws) {
     out->skey = reinterpret_cast<uint32_t*>(base + o_skey);
     out->sid = reinterpret_cast<uint32_t*>(base + o_sid);
     out->sort_tmp = base + o_tmp;
+    out->seg = reinterpret_cast<uint32_t*>(base + o_seg);
+    out->part = reinterpret_cast<float*>(base + o_part);
     out->sort_tmp_bytes = tmp;
   }
   return off;
@@ -627,11 +731,17 @@ static cudaError_t bwd_d(const AttnDev& a, cudaStream_t st) {
                                       end_bit, st);
   if (e != cudaSuccess) return e;
   const int64_t keys = (int64_t)a.B * a.n_kv * a.M;
-  const unsigned grid = (unsigned)((keys + 7) / 8);
-  if (a.d <= 32) { k_dkdv<DT, 1><<<grid, 256, 0, st>>>(a, E); note_launch(); }
-  else if (a.d <= 64) { k_dkdv<DT, 2><<<grid, 256, 0, st>>>(a, E); note_launch(); }
-  else if (a.d <= 128) { k_dkdv<DT, 4><<<grid, 256, 0, st>>>(a, E); note_launch(); }
-  else { k_dkdv<DT, 8><<<grid, 256, 0, st>>>(a, E); note_launch(); }
+  k_seg_starts<<<(unsigned)((keys + 1 + 255) / 256), 256, 0, st>>>(a, E);
+  note_launch();
+  const int64_t chunks = (E + kDkdvChunk - 1) / kDkdvChunk;
+  const unsigned grid = (unsigned)((chunks + 7) / 8);
+  if (chunks > 0) {
+    if (a.d <= 128) k_dkdv<DT, 4><<<grid, 256, 0, st>>>(a);
+    else k_dkdv<DT, 8><<<grid, 256, 0, st>>>(a);
+    note_launch();
+  }
+  k_dkdv_fix<DT><<<(unsigned)((keys + 7) / 8), 256, 0, st>>>(a);
+  note_launch();
   return cudaGetLastError();
 }
 

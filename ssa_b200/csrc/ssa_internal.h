@@ -112,6 +112,8 @@ struct AttnDev {
   uint32_t* eid;      // [rows][Kn] edge id (row * Kn + slot)
   uint32_t* skey;     // sorted keys
   uint32_t* sid;      // edge ids in sorted order
+  uint32_t* seg;      // [B*n_kv*M + 1] first sorted position of each key
+  float* part;        // [chunks][2][2][d] partial dk / dv of keys that cross a chunk edge
   void* sort_tmp;
   size_t sort_tmp_bytes;
 };
