@@ -456,6 +456,155 @@ __global__ void __launch_bounds__(256) k_attn_bwd_rows(AttnDev a) {
   }
 }
 
+// Backward, stage 1, vectorised (same conditions as k_attn_fwd_v16): the
+// row's slot keys staged in shared memory, 16-byte row gathers, U rows in
+// flight per 8-lane group, paired fp32 FMA.
+template <int DT, int EPL, bool FP32W, typename IT>
+__global__ void __launch_bounds__(256, (EPL >= 16 ? 2 : 3)) k_attn_bwd_rows_v16(AttnDev a) {
+  constexpr int U = 2;
+  extern __shared__ __align__(16) float s_all[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t i = (int64_t)blockIdx.x * 8 + warp;
+  if (i >= (int64_t)a.B * a.H * a.N) return;
+  int b, h, n, g;
+  decode_row(a, i, b, h, n, g);
+  const int Kp = (a.Kn + 31) & ~31;
+  float* sp = s_all + warp * 3 * Kp;  // p_j
+  float* sdp = sp + Kp;                // dP_j, then scale * dS_j
+  int* sk = reinterpret_cast<int*>(sdp + Kp);
+  const int grp = lane >> 3, li = lane & 7, e0 = li * EPL;
+  const int64_t row = ((int64_t)b * a.H + h) * a.N + n;
+  const void* nbr = static_cast<const char*>(a.nb) + row * a.Kn * (int64_t)sizeof(IT);
+  const uint8_t* vr = a.valid + row * a.Kn;
+  const void* kb = row_ptr<DT>(a.k, b * a.k_sb + g * a.k_sh);
+  const void* vb = row_ptr<DT>(a.v, b * a.v_sb + g * a.v_sh);
+  const int64_t orow_off = b * a.o_sb + h * a.o_sh + (int64_t)n * a.o_sn;
+
+  for (int j = lane; j < a.Kn; j += 32) sk[j] = slot_ok<IT>(a, nbr, vr, j) ? load_nb<IT>(nbr, j) : -1;
+  RawSlice<DT, EPL> qr, gr;
+  raw_load<DT, EPL>(row_ptr<DT>(a.q, b * a.q_sb + h * a.q_sh + (int64_t)n * a.q_sn), e0, qr);
+  raw_load<DT, EPL>(row_ptr<DT>(a.dO, orow_off), e0, gr);
+  unsigned long long q2[EPL / 2], g2[EPL / 2];
+#pragma unroll
+  for (int c = 0; c < EPL / 2; ++c) {
+    q2[c] = raw_pair<DT, EPL>(qr, c);
+    g2[c] = raw_pair<DT, EPL>(gr, c);
+  }
+  const float lse = a.lse_in[row];
+  __syncwarp();
+  for (int j0 = 0; j0 < a.Kn; j0 += 4 * U) {
+    RawSlice<DT, EPL> kr[U], vrw[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = j0 + u * 4 + grp;
+      const int key = j < a.Kn ? sk[j] : -1;
+      if (key >= 0) {
+        raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), e0, kr[u]);
+        raw_load<DT, EPL>(row_ptr<DT>(vb, (int64_t)key * a.v_sm), e0, vrw[u]);
+      } else {
+        raw_zero<DT, EPL>(kr[u]);
+        raw_zero<DT, EPL>(vrw[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      unsigned long long x2 = 0ull, y2 = 0ull;
+#pragma unroll
+      for (int c = 0; c < EPL / 2; ++c) {
+        x2 = f2_fma(q2[c], raw_pair<DT, EPL>(kr[u], c), x2);
+        y2 = f2_fma(g2[c], raw_pair<DT, EPL>(vrw[u], c), y2);
+      }
+      float xl, xh, yl, yh;
+      f2_unpack(x2, xl, xh);
+      f2_unpack(y2, yl, yh);
+      float ps = xl + xh, pd = yl + yh;
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        ps += __shfl_xor_sync(0xffffffffu, ps, o);
+        pd += __shfl_xor_sync(0xffffffffu, pd, o);
+      }
+      const int j = j0 + u * 4 + grp;
+      if (li == 0 && j < a.Kn) {
+        const bool ok = sk[j] >= 0;
+        sp[j] = ok ? expf(ps * a.scale - lse) : 0.f;
+        sdp[j] = ok ? pd : 0.f;
+      }
+    }
+  }
+  __syncwarp();
+  // Dropout: the gradient reaching the pre-dropout weights is dO.v_j scaled
+  // by 1/(1-p) where the weight was kept, 0 where it was dropped.
+  uint32_t keep_bits = 0xFFFFFFFFu;
+  if (a.drop_thresh) {
+    keep_bits = 0u;
+    for (int j = lane, kk = 0; j < a.Kn; j += 32, ++kk) {
+      const bool keep = dropout_keep((unsigned long long)row * a.Kn + j, a.drop_seed, a.drop_offset,
+                                     a.drop_thresh);
+      if (keep && kk < 32) keep_bits |= 1u << kk;
+      sdp[j] = keep ? sdp[j] * a.drop_scale : 0.f;
+    }
+    __syncwarp();
+  }
+  float dsum = 0.f;
+  for (int j = lane; j < a.Kn; j += 32) dsum = fmaf(sp[j], sdp[j], dsum);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, o);
+  const uint32_t BGM = (uint32_t)(a.B * a.n_kv) * (uint32_t)a.M;
+  const uint32_t bgM = (uint32_t)(b * a.n_kv + g) * (uint32_t)a.M;
+  for (int j = lane, kk = 0; j < a.Kn; j += 32, ++kk) {
+    const float p = sp[j];
+    const float ds = p * (sdp[j] - dsum) * a.scale;
+    const int64_t e = row * a.Kn + j;
+    const int key = sk[j];
+    float pv = (DT == kDtBF16 && !FP32W) ? round_bf16(p) : p;  // the weight that multiplied v_j
+    if (a.drop_thresh) {
+      const bool keep = kk < 32 ? ((keep_bits >> kk) & 1u) != 0
+                                : dropout_keep((unsigned long long)e, a.drop_seed, a.drop_offset, a.drop_thresh);
+      pv = keep ? ((DT == kDtBF16 && !FP32W) ? round_bf16(pv * a.drop_scale) : pv * a.drop_scale) : 0.f;
+    }
+    a.ep[e] = pv;
+    a.eds[e] = ds;
+    a.ekey[e] = key >= 0 ? bgM + (uint32_t)key : BGM;
+    a.eid[e] = (uint32_t)e;
+    sdp[j] = ds;
+  }
+  __syncwarp();
+  unsigned long long acc2[EPL / 2];
+#pragma unroll
+  for (int c = 0; c < EPL / 2; ++c) acc2[c] = 0ull;
+  for (int j0 = 0; j0 < a.Kn; j0 += 4 * U) {
+    RawSlice<DT, EPL> kr[U];
+    float ds[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = j0 + u * 4 + grp;
+      const int key = j < a.Kn ? sk[j] : -1;
+      ds[u] = key >= 0 ? sdp[j] : 0.f;
+      if (key >= 0) raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), e0, kr[u]);
+      else raw_zero<DT, EPL>(kr[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const unsigned long long dd = f2_pack(ds[u], ds[u]);
+#pragma unroll
+      for (int c = 0; c < EPL / 2; ++c) acc2[c] = f2_fma(dd, raw_pair<DT, EPL>(kr[u], c), acc2[c]);
+    }
+  }
+  float acc[EPL];
+#pragma unroll
+  for (int c = 0; c < EPL / 2; ++c) f2_unpack(acc2[c], acc[2 * c], acc[2 * c + 1]);
+#pragma unroll
+  for (int c = 0; c < EPL; ++c) {
+    acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], 8);
+    acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], 16);
+  }
+  if (grp == 0) {
+    void* dqr = row_ptr_mut<DT>(a.dq, orow_off);
+#pragma unroll
+    for (int c = 0; c < EPL; ++c) store1<DT>(dqr, e0 + c, acc[c]);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Backward, stage 3: one warp per (kv slice, key) sums its sorted segment.
 // ---------------------------------------------------------------------------
@@ -698,6 +847,19 @@ size_t attn_bwd_workspace_layout(const AttnDev& a, AttnDev* out, void* ws) {
 template <int DT, int EPL, bool FP32W, typename IT>
 static cudaError_t bwd_rows_t(const AttnDev& a, cudaStream_t st) {
   const int Kp = (a.Kn + 31) & ~31;
+  if constexpr (!(DT == kDtBF16 && EPL < 8) && EPL <= 16) {
+    if (fwd_vec16_ok<DT, EPL>(a) && (reinterpret_cast<uintptr_t>(a.dO) % 16) == 0 &&
+        ((a.o_sb | a.o_sh | a.o_sn) * (DT == kDtF32 ? 4 : 2)) % 16 == 0) {
+      const size_t smem = (size_t)8 * 3 * Kp * sizeof(float);
+      auto fn = k_attn_bwd_rows_v16<DT, EPL, FP32W, IT>;
+      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      const int64_t rows = (int64_t)a.B * a.H * a.N;
+      fn<<<(unsigned)((rows + 7) / 8), 256, smem, st>>>(a);
+      note_launch();
+      return cudaGetLastError();
+    }
+  }
   const size_t smem = (size_t)8 * 2 * Kp * sizeof(float);
   auto fn = k_attn_bwd_rows<DT, EPL, FP32W, IT>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
