@@ -44,7 +44,10 @@ def parse_args(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c5"])
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--mode", default="fwd", choices=["fwd", "train"],
+                    help="fwd: graph build + attention forward (the headline metric); train: "
+                         "graph build + attention forward + backward (one layer's attention core)")
     ap.add_argument("--impl", default="ssa", choices=["ssa", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -198,16 +201,24 @@ class _Job:
                 self.tokens_local = w.B * w.N
         del x, kv
 
-    def step(self, stream, mark):
+    def step(self, stream, mark, mark_bwd=None):
         """Runs one step; records `mark` (a CUDA event) between the graph
-        build and the attention where the plan has a single such point."""
+        build and the attention where the plan has a single such point.
+        With mark_bwd (training mode, single plan): the attention backward
+        follows the forward, and mark_bwd is recorded between them."""
         import torch
         from ssa_b200 import ops
         m, w = self.m, self.w
         if self.plan == "single":
             nb, valid = m._graph(self.q, self.k, w.M, self.causal, w.cross)
             mark.record(stream)
-            out, _ = ops.attn_fwd(self.q, self.k, self.v, nb, valid, m.scale, False, want_lse=False)
+            out, lse = ops.attn_fwd(self.q, self.k, self.v, nb, valid, m.scale, False,
+                                    want_lse=mark_bwd is not None)
+            if mark_bwd is not None:
+                mark_bwd.record(stream)
+                if getattr(self, "dO", None) is None:
+                    self.dO = torch.ones_like(out)
+                ops.attn_bwd(self.q, self.k, self.v, nb, valid, self.dO, lse, m.scale, False)
             return out
         if self.plan == "rows":
             k, v = self.runner.gather_kv(self.k_seq, self.v_seq)
@@ -245,15 +256,18 @@ def run_gpu(args):
     if args.batch:
         w = type(w)(**{**w.__dict__, "B": args.batch})
     plan = _plan(args, w, world)
+    if args.mode == "train" and plan != "single":
+        raise SystemExit("--mode train runs on one GPU (one layer's attention core)")
     m = make_module(w, dev)
     job = _Job(plan, w, m, dev, world, rank)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
     with torch.no_grad():
+        train = args.mode == "train"
         for _ in range(max(args.warmup, 0)):
             flush.zero_()
-            job.step(stream, torch.cuda.Event())
+            job.step(stream, torch.cuda.Event(), torch.cuda.Event() if train else None)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -267,20 +281,23 @@ def run_gpu(args):
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e2 = torch.cuda.Event(enable_timing=True)
+            eb = torch.cuda.Event(enable_timing=True) if train else None
             e0.record(stream)
-            job.step(stream, e1)
+            job.step(stream, e1, eb)
             e2.record(stream)
-            evs.append((e0, e1, e2))
+            evs.append((e0, e1, e2, eb))
         torch.cuda.synchronize()
         launches = _lib.load().ssa_kernel_launches() - launches0
         if world > 1:
             dist.barrier()
         clk = clocks.stop()
-    tot = [a.elapsed_time(c) for a, b, c in evs]
-    graph = [a.elapsed_time(b) for a, b, c in evs]
-    attn = [b.elapsed_time(c) for a, b, c in evs]
+    tot = [a.elapsed_time(c) for a, b, c, _ in evs]
+    graph = [a.elapsed_time(b) for a, b, c, _ in evs]
+    attn = [b.elapsed_time(eb if eb is not None else c) for a, b, c, eb in evs]
+    bwd = [eb.elapsed_time(c) for a, b, c, eb in evs if eb is not None]
     ms = statistics.mean(tot)
     ms_graph, ms_attn = statistics.mean(graph), statistics.mean(attn)
+    ms_bwd = statistics.mean(bwd) if bwd else None
     launches_all = launches
     if world > 1:
         t = torch.tensor([ms, ms_graph, ms_attn], device=dev)
@@ -306,13 +323,13 @@ def run_gpu(args):
     # End to end through the public API with host buffers: pinned q/k/v in,
     # attention output back to pinned host memory, copies inside the timing.
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and args.mode == "fwd":
         e2e = run_e2e(args, job, dev, flush, world)
 
     result = None
     if rank == 0:
         cpu = None
-        if not args.no_cpu_baseline and world == 1:
+        if not args.no_cpu_baseline and world == 1 and args.mode == "fwd":
             dt, desc, cores = cpu_sample(w, m, job.q, job.k, job.v, args.baseline_slices)
             val, _full = cpu_baseline_value(w, dt, args.baseline_slices)
             cpu = {"value": val, "unit": "tokens/s", "cores": cores, "kind": "port",
@@ -320,8 +337,10 @@ def run_gpu(args):
         par = {"single": "one GPU, whole job",
                "groups": f"group sharding: {w.B * w.n_kv} (batch, kv-head) units over {world} GPUs, no collective",
                "rows": f"query-row sharding: {w.N // world} rows per GPU, K/V all-gathered (NCCL)"}[plan]
+        metric = METRIC if args.mode == "fwd" else \
+            "sparse-attn train step (graph + attention fwd + bwd) tokens/s/GPU, one layer's attention core"
         result = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": w.dtype,
             "data": "synthetic (seeded N(0,1) activations; random-init weights in reference order)",
@@ -336,7 +355,8 @@ def run_gpu(args):
             "step_roofline": {"achieved": step_gbs, "frac": step_gbs / peak, "unit": "GB/s",
                               "note": "attention algorithmic bytes over graph build + attention, per GPU"},
             "kernels_ms": {"graph_build": ms_graph, "attention": ms_attn,
-                           "graph_build_per_step": [round(x, 3) for x in graph]},
+                           "graph_build_per_step": [round(x, 3) for x in graph],
+                           **({"attention_backward": ms_bwd} if ms_bwd is not None else {})},
             "gpu_launches": launches_all,
             "clocks": clk,
             "e2e": e2e,

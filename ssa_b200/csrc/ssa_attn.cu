@@ -636,7 +636,7 @@ __global__ void __launch_bounds__(256) k_seg_starts(AttnDev a, int64_t n_edges) 
 // a chunk edge leaves a partial (slot 0: it started before the chunk, slot
 // 1: it started inside), which k_dkdv_fix adds up in chunk order. The
 // result is deterministic.
-template <int DT, int EPW>
+template <int DT, int EPW, bool V16>
 __global__ void __launch_bounds__(256) k_dkdv(AttnDev a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t total = (int64_t)a.B * a.n_kv * a.M;
@@ -673,10 +673,20 @@ __global__ void __launch_bounds__(256) k_dkdv(AttnDev a) {
       rows_of(eb, qb, gb);
       float xq[2][EPW], xg[2][EPW];
       if (in_d) {
-        load_slice<DT, EPW>(qa, e0, a.d, xq[0]);
-        load_slice<DT, EPW>(ga, e0, a.d, xg[0]);
-        load_slice<DT, EPW>(qb, e0, a.d, xq[1]);
-        load_slice<DT, EPW>(gb, e0, a.d, xg[1]);
+        if constexpr (V16) {  // 16-byte aligned rows: one 16-byte load per 8 bf16
+#pragma unroll
+          for (int c = 0; c < EPW; c += 8) {
+            load8<DT>(qa, e0 + c, xq[0] + c);
+            load8<DT>(ga, e0 + c, xg[0] + c);
+            load8<DT>(qb, e0 + c, xq[1] + c);
+            load8<DT>(gb, e0 + c, xg[1] + c);
+          }
+        } else {
+          load_slice<DT, EPW>(qa, e0, a.d, xq[0]);
+          load_slice<DT, EPW>(ga, e0, a.d, xg[0]);
+          load_slice<DT, EPW>(qb, e0, a.d, xq[1]);
+          load_slice<DT, EPW>(gb, e0, a.d, xg[1]);
+        }
       }
       const float pa = __ldg(a.ep + ea), da = __ldg(a.eds + ea);
       const float pb = two ? __ldg(a.ep + eb) : 0.f, db = two ? __ldg(a.eds + eb) : 0.f;
@@ -898,8 +908,14 @@ static cudaError_t bwd_d(const AttnDev& a, cudaStream_t st) {
   const int64_t chunks = (E + kDkdvChunk - 1) / kDkdvChunk;
   const unsigned grid = (unsigned)((chunks + 7) / 8);
   if (chunks > 0) {
-    if (a.d <= 128) k_dkdv<DT, 4><<<grid, 256, 0, st>>>(a);
-    else k_dkdv<DT, 8><<<grid, 256, 0, st>>>(a);
+    // bf16 rows that are 16-byte aligned with d a multiple of 8: 16-byte loads
+    const int es = DT == kDtF32 ? 4 : 2;
+    auto al = [&](const void* p) { return (reinterpret_cast<uintptr_t>(p) % 16) == 0; };
+    const bool v16 = DT == kDtBF16 && a.d % 8 == 0 && al(a.q) && al(a.dO) &&
+                     ((a.q_sb | a.q_sh | a.q_sn | a.o_sb | a.o_sh | a.o_sn) * es) % 16 == 0;
+    if (v16) k_dkdv<DT, 8, true><<<grid, 256, 0, st>>>(a);
+    else if (a.d <= 128) k_dkdv<DT, 4, false><<<grid, 256, 0, st>>>(a);
+    else k_dkdv<DT, 8, false><<<grid, 256, 0, st>>>(a);
     note_launch();
   }
   k_dkdv_fix<DT><<<(unsigned)((keys + 7) / 8), 256, 0, st>>>(a);
