@@ -221,10 +221,14 @@ class _Job:
                 ops.attn_bwd(self.q, self.k, self.v, nb, valid, self.dO, lse, m.scale, False)
             return out
         if self.plan == "rows":
-            k, v = self.runner.gather_kv(self.k_seq, self.v_seq)
+            from ssa_b200.sharding import gather_seq_major, seq_major_view
+            k = seq_major_view(gather_seq_major(self.k_seq, self.runner.group))
+            v_full, v_work = gather_seq_major(self.v_seq, self.runner.group, async_op=True)
             nb, valid = m._graph(self.q, k, w.N, self.causal, False, q_row0=self.runner.rows[0])
             mark.record(stream)
-            out, _ = ops.attn_fwd(self.q, k, v, nb, valid, m.scale, False, want_lse=False)
+            v_work.wait()
+            out, _ = ops.attn_fwd(self.q, k, seq_major_view(v_full), nb, valid, m.scale, False,
+                                  want_lse=False)
             return out
         rep = w.H // w.n_kv
         from ssa_b200.sharding import slice_views

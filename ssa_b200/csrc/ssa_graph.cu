@@ -102,11 +102,35 @@ __global__ void __launch_bounds__(256) k_hash_keys(GraphDev g) {
 // ---------------------------------------------------------------------------
 // 2. Keep the first C members of every bucket (stable order), sizes, C-th member
 // ---------------------------------------------------------------------------
+// One warp per (b, kv head, round, bucket): lane L owns a contiguous run of
+// the bucket's 64-key mask words; a warp prefix sum of their popcounts gives
+// every word's rank, so members past the first C are cleared in parallel.
+// bsize = the bucket's full size; lastc = the key at rank min(size, C) - 1
+// (-1 for an empty bucket). The first warp of each (b, kv head, round) also
+// marks its pad key perm_r[M-1] in pmask.
 __global__ void __launch_bounds__(256) k_bucket_trim(GraphDev g) {
-  const int bg = blockIdx.x / g.R, r = blockIdx.x % g.R;
-  for (int u = threadIdx.x; u < g.NB; u += blockDim.x) {
-    int run = 0, last = -1;
-    for (int w = 0; w < g.W; ++w) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (wid >= (int64_t)g.B * g.n_kv * g.R * g.NB) return;
+  const int u = (int)(wid % g.NB);
+  const int64_t t = wid / g.NB;
+  const int r = (int)(t % g.R), bg = (int)(t / g.R);
+  const int wpl = (g.W + 31) / 32;
+  const int w0 = min(lane * wpl, g.W), w1 = min(w0 + wpl, g.W);
+  int cnt = 0;
+  for (int w = w0; w < w1; ++w) cnt += __popcll(g.bmap[bmap_idx(g, bg, w, r, u)]);
+  int incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  const int size = __shfl_sync(0xffffffffu, incl, 31);
+  const int keep_n = min(size, g.C);  // members that stay
+  int run = incl - cnt;               // members before this lane's words
+  int last = -1;
+  if (run < keep_n || size > g.C) {
+    for (int w = w0; w < w1; ++w) {
       unsigned long long* ptr = &g.bmap[bmap_idx(g, bg, w, r, u)];
       unsigned long long x = *ptr;
       if (!x) continue;
@@ -115,25 +139,31 @@ __global__ void __launch_bounds__(256) k_bucket_trim(GraphDev g) {
         *ptr = 0ull;
       } else if (run + c > g.C) {
         int need = g.C - run;
-        unsigned long long keep = 0ull;
+        unsigned long long kept = 0ull;
         while (need--) {
           const unsigned long long lo = x & (~x + 1ull);
-          keep |= lo;
+          kept |= lo;
           x ^= lo;
         }
-        *ptr = keep;
-        last = w * 64 + 63 - __clzll(keep);
+        *ptr = kept;
+        last = w * 64 + 63 - __clzll(kept);
       } else {
         last = w * 64 + 63 - __clzll(x);
       }
       run += c;
     }
-    g.bsize[(bg * g.R + r) * g.NB + u] = run;
-    g.lastc[(bg * g.R + r) * g.NB + u] = last;
   }
-  if (threadIdx.x == 0) {
-    const uint32_t P = g.pmax[bg * g.R + r] & 0xFFFFFu;
-    atomicOr(&g.pmask[(int64_t)bg * g.Wpad + (P >> 6)], 1ull << (P & 63));
+  // the bucket's last kept member lies in the highest lane that kept one
+  const unsigned has = __ballot_sync(0xffffffffu, last >= 0);
+  const int src = has ? 31 - __clz(has) : 0;
+  last = __shfl_sync(0xffffffffu, last, src);
+  if (lane == 0) {
+    g.bsize[(bg * g.R + r) * g.NB + u] = size;
+    g.lastc[(bg * g.R + r) * g.NB + u] = has ? last : -1;
+    if (u == 0) {
+      const uint32_t P = g.pmax[bg * g.R + r] & 0xFFFFFu;
+      atomicOr(&g.pmask[(int64_t)bg * g.Wpad + (P >> 6)], 1ull << (P & 63));
+    }
   }
 }
 
@@ -498,7 +528,10 @@ cudaError_t launch_graph(const GraphDev& g, int mode, cudaStream_t st) {
     note_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  k_bucket_trim<<<g.B * g.n_kv * g.R, 256, 0, st>>>(g);
+  {
+    const int64_t warps = (int64_t)g.B * g.n_kv * g.R * g.NB;
+    k_bucket_trim<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(g);
+  }
   note_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   GraphDev f = g;

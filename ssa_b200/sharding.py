@@ -77,16 +77,18 @@ def slice_views(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, s: GroupSlice
     return (q[s.b0:s.b1, s.g0 * rep:s.g1 * rep], k[s.b0:s.b1, s.g0:s.g1], v[s.b0:s.b1, s.g0:s.g1])
 
 
-def gather_seq_major(local: torch.Tensor, group=None) -> torch.Tensor:
+def gather_seq_major(local: torch.Tensor, group=None, async_op: bool = False):
     """All-gather of sequence-major rows: local (m, ...) from every rank,
-    rank order, into one (world * m, ...) tensor."""
+    rank order, into one (world * m, ...) tensor. With async_op, returns
+    (tensor, work); work.wait() orders later work on the current stream
+    after the transfer."""
     import torch.distributed as dist
     world = dist.get_world_size(group)
     local = local.contiguous()
     out = torch.empty((world * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
                       device=local.device)
-    dist.all_gather_into_tensor(out, local, group=group)
-    return out
+    work = dist.all_gather_into_tensor(out, local, group=group, async_op=async_op)
+    return (out, work) if async_op else out
 
 
 def seq_major_view(x: torch.Tensor) -> torch.Tensor:
@@ -163,7 +165,10 @@ class RowSharded:
 
     def step(self, q_local: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor):
         """q_local (B,H,n,d) for rows [r0, r1); k_local, v_local (m,B,n_kv,d).
-        Returns this rank's attention output (B,H,n,d)."""
-        k, v = self.gather_kv(k_local, v_local)
+        Returns this rank's attention output (B,H,n,d). The values' all-gather
+        runs while the graph is built; only the attention waits for it."""
+        k = seq_major_view(gather_seq_major(k_local, self.group))
+        v_full, v_work = gather_seq_major(v_local, self.group, async_op=True)
         nb, valid = self.graph_fn(q_local, k, self.N, self.causal, False, self.rows[0])
-        return self.attn_fn(q_local, k, v, nb, valid)
+        v_work.wait()
+        return self.attn_fn(q_local, k, seq_major_view(v_full), nb, valid)
