@@ -52,20 +52,20 @@ __global__ void __launch_bounds__(256) k_hash_keys(GraphDev g) {
     const int r = i / pd, rem = i - r * pd;
     s_planes[i] = g.rp[(int64_t)r * g.max_p * g.d + rem];
   }
+  __shared__ uint32_t s_pmax[8][64];  // per warp and round (R <= 64): packed max, reduced per block
   __syncthreads();
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
   const bool act = m < g.M;
   const unsigned amask = __ballot_sync(0xffffffffu, act);
-  if (!act) return;
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int wbase = m - lane;  // multiple of 32
   // The key row stays in registers for all R * p projections.
   float x[D];
-  const void* row = row_ptr<DT>(g.k, b * g.k_sb + gk * g.k_sh + (int64_t)m * g.k_sm);
+  const void* row = row_ptr<DT>(g.k, b * g.k_sb + gk * g.k_sh + (int64_t)(act ? m : 0) * g.k_sm);
 #pragma unroll
   for (int i = 0; i < D; i += 4) {
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (i < g.d) v = load4<DT>(row, i);
+    if (act && i < g.d) v = load4<DT>(row, i);
     x[i] = v.x; x[i + 1] = v.y; x[i + 2] = v.z; x[i + 3] = v.w;
   }
   for (int r = 0; r < g.R; ++r) {
@@ -86,16 +86,25 @@ __global__ void __launch_bounds__(256) k_hash_keys(GraphDev g) {
       f2_unpack(s2, s0, s1);
       if (s0 + s1 > 0.f) code |= 1u << j;  // proj > 0, strict (:589)
     }
-    g.kcode[((int64_t)bg * g.R + r) * g.M + m] = (uint16_t)code;
-    const unsigned peers = __match_any_sync(amask, code);
-    if (lane == __ffs(peers) - 1) {
-      const unsigned long long bits = (unsigned long long)peers << (wbase & 63);
-      atomicOr(&g.bmap[bmap_idx(g, bg, wbase >> 6, r, (int)code)], bits);
+    uint32_t mx = 0u;
+    if (act) {
+      g.kcode[((int64_t)bg * g.R + r) * g.M + m] = (uint16_t)code;
+      const unsigned peers = __match_any_sync(amask, code);
+      if (lane == __ffs(peers) - 1) {
+        const unsigned long long bits = (unsigned long long)peers << (wbase & 63);
+        atomicOr(&g.bmap[bmap_idx(g, bg, wbase >> 6, r, (int)code)], bits);
+      }
+      // perm[M-1] of the stable sort = largest key of the highest bucket.
+      mx = __reduce_max_sync(amask, (code << 20) | (uint32_t)m);
     }
-    // perm[M-1] of the stable sort = largest key of the highest bucket.
-    const uint32_t packed = (code << 20) | (uint32_t)m;
-    const uint32_t mx = __reduce_max_sync(amask, packed);
-    if (lane == __ffs(amask) - 1) atomicMax(&g.pmax[bg * g.R + r], mx);
+    if (lane == 0) s_pmax[warp][r] = mx;
+  }
+  // one atomicMax per block and round instead of one per warp
+  __syncthreads();
+  if (threadIdx.x < g.R) {
+    uint32_t mx = 0u;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) mx = max(mx, s_pmax[w][threadIdx.x]);
+    atomicMax(&g.pmax[bg * g.R + threadIdx.x], mx);
   }
 }
 
