@@ -205,6 +205,17 @@ SSA_API int ssa_attn_bwd_noalloc(const ssa_attn_params* p, const void* q, const 
                                  const void* dO, const float* lse, void* dq, void* dk, void* dv,
                                  void* stream);
 
+/*
+ * neighbor_overlap (sparse_attention.py:1583-1615): per row, the Jaccard
+ * similarity of two neighbor sets -- the number of valid A slots whose index
+ * is among the valid B slots, over |valid A| + |valid B| minus that number
+ * (at least 1). nb_a, nb_b (rows, K) int32 (nb_i64 = 0) or int64; valid_a,
+ * valid_b (rows, K) uint8/bool; out (rows,) fp32. K <= 2048.
+ */
+SSA_API int ssa_neighbor_overlap(const void* nb_a, const uint8_t* valid_a, const void* nb_b,
+                                 const uint8_t* valid_b, int64_t rows, int32_t K, int32_t nb_i64,
+                                 float* out, void* stream);
+
 /* Error code recorded by a kernel whose bounded wait on an on-chip barrier
  * ran out (0 = none); synchronises with the device. clear != 0 resets it. */
 SSA_API int32_t ssa_device_error(int32_t clear);

@@ -63,6 +63,7 @@ SIGNATURES = {
                                     _vp, _vp, _vp, _vp, _sz, _vp]),
     "ssa_attn_bwd_noalloc": (ctypes.c_int, [ctypes.POINTER(AttnParams), _vp, _vp, _vp, _vp, _vp, _vp,
                                             _vp, _vp, _vp, _vp, _vp]),
+    "ssa_neighbor_overlap": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp]),
     "ssa_device_error": (_i32, [_i32]),
     "ssa_last_error": (ctypes.c_char_p, []),
     "ssa_abi_version": (_i32, []),

@@ -424,13 +424,9 @@ class SparseTransformer(nn.Module):
 def neighbor_overlap(neighbors_a: torch.Tensor, neighbors_b: torch.Tensor,
                      valid_a: torch.Tensor, valid_b: torch.Tensor) -> torch.Tensor:
     """Per-(b, h, query) Jaccard similarity of two neighbor sets, padding
-    ignored (diagnostic, sparse_attention.py:1583-1615)."""
-    a = torch.where(valid_a, neighbors_a, torch.full_like(neighbors_a, -1))
-    b = torch.where(valid_b, neighbors_b, torch.full_like(neighbors_b, -1))
-    a_in_b = (a.unsqueeze(-1) == b.unsqueeze(-2)).any(dim=-1) & valid_a
-    inter = a_in_b.sum(dim=-1).float()
-    union = (valid_a.sum(dim=-1) + valid_b.sum(dim=-1)).float() - inter
-    return inter / union.clamp_min(1.0)
+    ignored (diagnostic, sparse_attention.py:1583-1615), as one CUDA kernel:
+    no (B, H, N, K, K) match tensor."""
+    return ops.neighbor_overlap(neighbors_a, neighbors_b, valid_a, valid_b)
 
 
 def measure_cross_layer_overlap(model: "SparseTransformer", x: torch.Tensor) -> dict:

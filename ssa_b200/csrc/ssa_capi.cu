@@ -128,7 +128,7 @@ extern "C" {
 
 const char* ssa_last_error(void) { return g_err; }
 
-int32_t ssa_abi_version(void) { return 103; }
+int32_t ssa_abi_version(void) { return 104; }
 
 int32_t ssa_device_error(int32_t clear) { return ssa::read_device_error(clear); }
 
@@ -300,6 +300,20 @@ int ssa_attn_bwd(const ssa_attn_params* p, const void* q, const void* k, const v
 // Attention backward without a caller workspace: the scratch is a file-scope
 // device array, one per device, whose address the host resolves once.
 // ---------------------------------------------------------------------------
+int ssa_neighbor_overlap(const void* nb_a, const uint8_t* valid_a, const void* nb_b, const uint8_t* valid_b,
+                         int64_t rows, int32_t K, int32_t nb_i64, float* out, void* stream) {
+  if (rows < 0 || K < 1) return fail(SSA_ERR_INVALID, "rows=%lld, K=%d", (long long)rows, K);
+  if (rows == 0) return SSA_OK;
+  if (!nb_a || !valid_a || !nb_b || !valid_b || !out) return fail(SSA_ERR_INVALID, "NULL pointer");
+  if (K > 2048) return fail(SSA_ERR_UNSUPPORTED, "neighbor_overlap supports K <= 2048 (got %d)", K);
+  const size_t isz = nb_i64 ? 8 : 4;
+  if (!aligned(nb_a, isz) || !aligned(nb_b, isz)) return fail(SSA_ERR_INVALID, "neighbor arrays misaligned");
+  cudaError_t e = ssa::launch_neighbor_overlap(nb_a, valid_a, nb_b, valid_b, rows, K, nb_i64, out,
+                                               static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "neighbor_overlap launch");
+  return SSA_OK;
+}
+
 int64_t ssa_kernel_launches(void) { return ssa::g_kernel_launches.load(std::memory_order_relaxed); }
 
 }  // extern "C"

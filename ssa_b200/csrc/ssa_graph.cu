@@ -408,6 +408,46 @@ __global__ void __launch_bounds__(256) k_hash_ids(const void* x, int B, int head
 }
 
 // ---------------------------------------------------------------------------
+// neighbor_overlap (sparse_attention.py:1583-1615): per row, the number of
+// valid A slots whose index is among the valid B slots, over |valid A| +
+// |valid B| - that number (at least 1). One warp per row: B's valid indices
+// staged in shared memory, each lane tests its A slots against all of them
+// (broadcast reads, exact for any order and duplicates).
+// ---------------------------------------------------------------------------
+template <typename IT>
+__global__ void __launch_bounds__(256) k_neighbor_overlap(const IT* nb_a, const uint8_t* va, const IT* nb_b,
+                                                          const uint8_t* vb, int64_t rows, int K, float* out) {
+  extern __shared__ __align__(16) long long s_b[];  // [8 warps][K]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + warp;
+  if (row >= rows) return;
+  long long* sb = s_b + (size_t)warp * K;
+  const IT* ra = nb_a + row * K;
+  const IT* rb = nb_b + row * K;
+  int nbv = 0;  // valid B slots
+  for (int j0 = 0; j0 < K; j0 += 32) {
+    const int j = j0 + lane;
+    const bool v = j < K && __ldg(vb + row * K + j);
+    const unsigned m = __ballot_sync(0xffffffffu, v);
+    if (v) sb[nbv + __popc(m & ((1u << lane) - 1u))] = (long long)__ldg(rb + j);
+    nbv += __popc(m);
+  }
+  __syncwarp();
+  int inter = 0, nav = 0;
+  for (int j = lane; j < K; j += 32) {
+    if (!__ldg(va + row * K + j)) continue;
+    ++nav;
+    const long long x = (long long)__ldg(ra + j);
+    bool hit = false;
+    for (int z = 0; z < nbv && !hit; ++z) hit = sb[z] == x;
+    inter += hit ? 1 : 0;
+  }
+  inter = __reduce_add_sync(0xffffffffu, inter);
+  nav = __reduce_add_sync(0xffffffffu, nav);
+  if (lane == 0) out[row] = (float)inter / fmaxf((float)(nav + nbv - inter), 1.f);
+}
+
+// ---------------------------------------------------------------------------
 // Host launchers
 // ---------------------------------------------------------------------------
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -579,6 +619,24 @@ cudaError_t launch_hash_ids(const void* x, int dtype, int B, int heads, int rows
     k_hash_ids<kDtF32><<<grid, 256, 0, st>>>(x, B, heads, rows, d, sb, sh, sn, rp, R, max_p, p, out);
   else
     k_hash_ids<kDtBF16><<<grid, 256, 0, st>>>(x, B, heads, rows, d, sb, sh, sn, rp, R, max_p, p, out);
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_neighbor_overlap(const void* nb_a, const uint8_t* va, const void* nb_b, const uint8_t* vb,
+                                    int64_t rows, int K, int nb_i64, float* out, cudaStream_t st) {
+  const size_t smem = (size_t)8 * K * sizeof(long long);
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  cudaError_t e;
+  if (nb_i64) {
+    if ((e = set_smem(k_neighbor_overlap<int64_t>, smem)) != cudaSuccess) return e;
+    k_neighbor_overlap<int64_t><<<grid, 256, smem, st>>>(static_cast<const int64_t*>(nb_a), va,
+                                                         static_cast<const int64_t*>(nb_b), vb, rows, K, out);
+  } else {
+    if ((e = set_smem(k_neighbor_overlap<int32_t>, smem)) != cudaSuccess) return e;
+    k_neighbor_overlap<int32_t><<<grid, 256, smem, st>>>(static_cast<const int32_t*>(nb_a), va,
+                                                         static_cast<const int32_t*>(nb_b), vb, rows, K, out);
+  }
   note_launch();
   return cudaGetLastError();
 }

@@ -70,6 +70,8 @@ cudaError_t launch_hash_queries(const GraphDev& g, cudaStream_t st);
 cudaError_t launch_rows(const GraphDev& g, int stage, int mode, cudaStream_t st);
 size_t rows_smem_bytes(const GraphDev& g, int warps);
 int read_device_error(int clear);
+cudaError_t launch_neighbor_overlap(const void* nb_a, const uint8_t* va, const void* nb_b, const uint8_t* vb,
+                                    int64_t rows, int K, int nb_i64, float* out, cudaStream_t st);
 struct MergeDev {
   int B, H, N, A, Kw, G, Wout;
   const int32_t* lsh;       // [B][H][N][A]

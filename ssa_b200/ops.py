@@ -314,3 +314,24 @@ def gather_attention(q, k, v, nb, valid, scale: float, fp32w: bool = False, drop
     if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
         return GatherAttention.apply(q, k, v, nb, valid, scale, fp32w, dropout)
     return attn_fwd(q, k, v, nb, valid, scale, fp32w, want_lse=False, dropout=dropout)[0]
+
+
+def neighbor_overlap(nb_a: torch.Tensor, nb_b: torch.Tensor, valid_a: torch.Tensor,
+                     valid_b: torch.Tensor) -> torch.Tensor:
+    """Per-row Jaccard similarity of two (..., K) neighbor-set tensors on the
+    GPU; returns fp32 of shape nb_a.shape[:-1]."""
+    _require_cuda(nb_a, nb_b, valid_a, valid_b)
+    if nb_a.shape != nb_b.shape or valid_a.shape != nb_a.shape or valid_b.shape != nb_a.shape:
+        raise ValueError("neighbor_overlap: all four tensors must have one shape")
+    K = nb_a.shape[-1]
+    rows = nb_a.numel() // K
+    i64 = nb_a.dtype == torch.int64 or nb_b.dtype == torch.int64
+    dt = torch.int64 if i64 else torch.int32
+    a = nb_a.to(dt).contiguous()
+    b = nb_b.to(dt).contiguous()
+    va = valid_a.to(torch.uint8).contiguous()
+    vb = valid_b.to(torch.uint8).contiguous()
+    out = torch.empty(nb_a.shape[:-1], dtype=torch.float32, device=nb_a.device)
+    check(_lib.load().ssa_neighbor_overlap(_ptr(a), _ptr(va), _ptr(b), _ptr(vb), rows, K, int(i64),
+                                           _ptr(out), _stream(nb_a.device)), "ssa_neighbor_overlap")
+    return out
