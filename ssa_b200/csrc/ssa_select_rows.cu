@@ -201,7 +201,7 @@ __device__ __forceinline__ uint32_t warp_sort_desc(uint32_t v) {
   return v;
 }
 
-// The kth largest (1-based) order key among the participants of sc[0..n):
+// The kth largest (1-based) order key among the participants of ok[0..n):
 // entries whose order key is >= lo (all entries if fewer than kth qualify).
 // Each round histograms the participants of the current key range [ulo, uhi]
 // into 256 bins of width 2^s (s the smallest shift that fits the range) and
@@ -209,17 +209,17 @@ __device__ __forceinline__ uint32_t warp_sort_desc(uint32_t v) {
 // 32 entries they are sorted across the warp. Returns the key T and, in
 // *need, how many entries equal to T belong to the top kth. `list` holds 32
 // entries. Warp-collective.
-__device__ uint32_t warp_select_kth(const float* sc, int n, int kth, uint32_t lo, uint32_t* hist,
+__device__ uint32_t warp_select_kth(const uint32_t* ok, int n, int kth, uint32_t lo, uint32_t* hist,
                                     uint32_t* list, int* need_out) {
   const int lane = threadIdx.x & 31;
   uint32_t mx = 0u, mn = 0xFFFFFFFFu, cntp = 0u;
   for (int i = lane; i < n; i += 32) {
-    const uint32_t u = okey(sc[i]);
+    const uint32_t u = ok[i];
     if (u >= lo) { mx = max(mx, u); mn = min(mn, u); ++cntp; }
   }
   if ((int)__reduce_add_sync(0xffffffffu, cntp) < kth) {
     mx = 0u; mn = 0xFFFFFFFFu;
-    for (int i = lane; i < n; i += 32) { const uint32_t u = okey(sc[i]); mx = max(mx, u); mn = min(mn, u); }
+    for (int i = lane; i < n; i += 32) { const uint32_t u = ok[i]; mx = max(mx, u); mn = min(mn, u); }
   }
   uint32_t uhi = __reduce_max_sync(0xffffffffu, mx);
   uint32_t ulo = __reduce_min_sync(0xffffffffu, mn);
@@ -233,7 +233,7 @@ __device__ uint32_t warp_select_kth(const float* sc, int n, int kth, uint32_t lo
     for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0;
     __syncwarp();
     for (int i = lane; i < n; i += 32) {
-      const uint32_t u = okey(sc[i]);
+      const uint32_t u = ok[i];
       if (u >= ulo && u <= uhi) atomicAdd(&hist[(u - ulo) >> sh], 1u);
     }
     __syncwarp();
@@ -280,7 +280,7 @@ __device__ uint32_t warp_select_kth(const float* sc, int n, int kth, uint32_t lo
         uint32_t u = 0u;
         bool m = false;
         if (i < n) {
-          u = okey(sc[i]);
+          u = ok[i];
           m = u >= ulo && u <= uhi;
         }
         const unsigned bm = __ballot_sync(0xffffffffu, m);
@@ -301,7 +301,7 @@ __device__ uint32_t warp_select_kth(const float* sc, int n, int kth, uint32_t lo
 }
 
 struct RowsSmem {
-  float* sc;        // [max(cap, Wout)] scores; later the staged neighbor row
+  uint32_t* ok;     // [max(cap, Wout)] order keys of the scores; later the staged neighbor row
   uint16_t* ky;     // [cap] keys (the tensor-core path has M <= 65536)
   uint32_t* hist;   // [256]
   uint32_t* bits;   // [Mw] merge bitmap over [0, M)
@@ -343,8 +343,8 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
     S.hist = reinterpret_cast<uint32_t*>(base);
     tcache = reinterpret_cast<uint16_t*>(S.hist + 256);
   } else {
-    S.sc = reinterpret_cast<float*>(base);
-    S.ky = reinterpret_cast<uint16_t*>(S.sc + scn);
+    S.ok = reinterpret_cast<uint32_t*>(base);
+    S.ky = reinterpret_cast<uint16_t*>(S.ok + scn);
     S.hist = reinterpret_cast<uint32_t*>(base + (size_t)scn * 4 + (((size_t)cap * 2 + 15) & ~size_t(15)));
     S.bits = S.hist + 256;
     S.l1 = S.bits + Mw;
@@ -402,7 +402,7 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
     const int c = cnt_all;
     for (int i = lane; i < c; i += 32) {
       const unsigned long long e = __ldcs(bo + (i < cnt0 ? i : half_cap + i - cnt0));  // read once
-      S.sc[i] = __uint_as_float((uint32_t)e);
+      S.ok[i] = okey(__uint_as_float((uint32_t)e));
       S.ky[i] = (uint16_t)(e >> 32);
     }
     // Special keys: pad keys perm_r[M-1], causal self, empty-bucket fallbacks.
@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
         acc += __shfl_xor_sync(0xffffffffu, acc, 2);
         acc += __shfl_xor_sync(0xffffffffu, acc, 4);
         if (j < ndot && sub == 0) {
-          S.sc[c + j] = acc;
+          S.ok[c + j] = okey(acc);
           S.ky[c + j] = (uint16_t)S.spec[32 + j];
         }
       }
@@ -563,16 +563,15 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
       const float tz = tau == 0.f ? -0.f : tau;
       const uint32_t lo = tau > -INFINITY ? okey(tz) : 0u;
       int need;
-      const uint32_t T = warp_select_kth(S.sc, tot, g.A, lo, S.hist, reinterpret_cast<uint32_t*>(S.spec), &need);
+      const uint32_t T = warp_select_kth(S.ok, tot, g.A, lo, S.hist, reinterpret_cast<uint32_t*>(S.spec), &need);
       // Compact the selection to the front: keys > T, then `need` keys == T
       // in index order (ties are the reference's unspecified topk order).
       int wpos = 0, eq_seen = 0;
       for (int i0 = 0; i0 < tot; i0 += 32) {
         const int i = i0 + lane;
         const bool in = i < tot;
-        const float sv = in ? S.sc[i] : 0.f;
+        const uint32_t u = in ? S.ok[i] : 0u;
         const uint16_t kv = in ? S.ky[i] : 0;
-        const uint32_t u = okey(sv);
         const bool eq = in && u == T;
         const unsigned eqm = __ballot_sync(0xffffffffu, eq);
         const int eq_rank = eq_seen + __popc(eqm & ((1u << lane) - 1u));
@@ -581,7 +580,7 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
         __syncwarp();
         if (sel) {
           const int dst = wpos + __popc(sm & ((1u << lane) - 1u));
-          S.sc[dst] = sv;
+          S.ok[dst] = u;
           S.ky[dst] = kv;
         }
         __syncwarp();
@@ -593,11 +592,12 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
 
     if (mode == 1) {
       // Reference topk order: descending score. Bitonic sort of n_elig
-      // entries (padded to a power of two with -inf) in shared memory.
+      // entries by order key (padded to a power of two with key 0, below
+      // every score's) in shared memory.
       int P2 = 32;
       while (P2 < n_elig) P2 <<= 1;
       for (int i = n_elig + lane; i < P2; i += 32) {
-        S.sc[i] = -INFINITY;
+        S.ok[i] = 0u;
         S.ky[i] = 0xFFFF;
       }
       __syncwarp();
@@ -607,10 +607,10 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
             const int ixj = i ^ j2;
             if (ixj > i) {
               const bool desc = (i & k2) == 0;
-              const float a = S.sc[i], bb = S.sc[ixj];
+              const uint32_t a = S.ok[i], bb = S.ok[ixj];
               if ((a < bb) == desc) {
-                S.sc[i] = bb;
-                S.sc[ixj] = a;
+                S.ok[i] = bb;
+                S.ok[ixj] = a;
                 const uint16_t t0 = S.ky[i];
                 S.ky[i] = S.ky[ixj];
                 S.ky[ixj] = t0;
@@ -689,7 +689,7 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
     const int nlg = __shfl_sync(0xffffffffu, incl, 31);
     const int nbelow = __reduce_add_sync(0xffffffffu, below);
     const int s0 = g.is_cross ? 0 : 1;
-    int* stage_out = reinterpret_cast<int*>(S.sc);  // the scores are no longer needed
+    int* stage_out = reinterpret_cast<int*>(S.ok);  // the scores are no longer needed
     __syncwarp();
     if (w0 < w1) {
       int rank = incl - cnt;
