@@ -154,6 +154,64 @@ __device__ __forceinline__ float dot_row_global(const float* q, const void* row,
   return (s0 + s1) + (s2 + s3);
 }
 
+// Projections of one row (x: D floats in registers, zero beyond d) onto NBK
+// hyperplanes pl, pl + d, ..., pl + (NBK-1) d. Each projection takes the same
+// operations in the same order as a lone dot product would -- even elements
+// accumulate into the low half of a paired fp32 FMA, odd ones into the high
+// half, in element order, and the projection is the sum of the halves -- so
+// the result is bit-identical however many hyperplanes share the pass; the
+// NBK chains only give the FMA pipe independent work.
+template <int NBK, int D, bool SMEM>
+__device__ __forceinline__ void proj_planes(const float* x, const float* pl, int d, float* out) {
+  unsigned long long s2[NBK];
+#pragma unroll
+  for (int k = 0; k < NBK; ++k) s2[k] = 0ull;
+#pragma unroll
+  for (int t = 0; t < D; t += 4) {
+    if (t < d) {
+      const unsigned long long xa = f2_pack(x[t], x[t + 1]), xb = f2_pack(x[t + 2], x[t + 3]);
+#pragma unroll
+      for (int k = 0; k < NBK; ++k) {
+        const float4 w = SMEM ? *reinterpret_cast<const float4*>(pl + k * d + t)
+                              : __ldg(reinterpret_cast<const float4*>(pl + k * d + t));
+        s2[k] = f2_fma(xa, f2_pack(w.x, w.y), s2[k]);
+        s2[k] = f2_fma(xb, f2_pack(w.z, w.w), s2[k]);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < NBK; ++k) {
+    float s0, s1;
+    f2_unpack(s2[k], s0, s1);
+    out[k] = s0 + s1;
+  }
+}
+
+// f(j, proj_j) for the hyperplanes j = 0 .. p-1 of one round (hyperplane j
+// at pl + j d): four per pass while four remain, then two, then one.
+template <int D, bool SMEM, typename F>
+__device__ __forceinline__ void for_round_projections(const float* x, const float* pl, int d, int p, F&& f) {
+  int j = 0;
+  for (; j + 4 <= p; j += 4) {
+    float o[4];
+    proj_planes<4, D, SMEM>(x, pl + (size_t)j * d, d, o);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) f(j + k, o[k]);
+  }
+  if (j + 2 <= p) {
+    float o[2];
+    proj_planes<2, D, SMEM>(x, pl + (size_t)j * d, d, o);
+    f(j, o[0]);
+    f(j + 1, o[1]);
+    j += 2;
+  }
+  if (j < p) {
+    float o[1];
+    proj_planes<1, D, SMEM>(x, pl + (size_t)j * d, d, o);
+    f(j, o[0]);
+  }
+}
+
 // The row's bucket id per (round, probe) slot into tids (sign tests in fp32,
 // sparse_attention.py:559-597; step-wise multi-probe, :599-646: probe t flips
 // the bit with the t-th smallest |proj| of the ORIGINAL id, ties in plane
@@ -168,29 +226,14 @@ __device__ inline bool hash_row_ids(const GraphDev& g, const float* q, int bg, u
 #pragma unroll
     for (int j = 0; j < 12; ++j) proj[j] = 0.f;
     uint32_t id = 0;
-    for (int j = 0; j < g.p; ++j) {
-      const float* pl = g.rp + ((int64_t)r * g.max_p + j) * g.d;
-      // Even elements accumulate into the low half, odd ones into the high
-      // half, in element order; the projection is their sum.
-      unsigned long long s2 = 0ull;
-#pragma unroll
-      for (int i = 0; i < D; i += 4) {
-        if (i < g.d) {
-          const float4 w = __ldg(reinterpret_cast<const float4*>(pl + i));
-          s2 = f2_fma(f2_pack(q[i], q[i + 1]), f2_pack(w.x, w.y), s2);
-          s2 = f2_fma(f2_pack(q[i + 2], q[i + 3]), f2_pack(w.z, w.w), s2);
-        }
-      }
-      float s0, s1;
-      f2_unpack(s2, s0, s1);
-      const float s = s0 + s1;
+    for_round_projections<D, false>(q, g.rp + (int64_t)r * g.max_p * g.d, g.d, g.p, [&](int j, float s) {
       if (s > 0.f) id |= 1u << j;
       if (g.Te > 0) {
 #pragma unroll
         for (int jj = 0; jj < 12; ++jj)
           if (jj == j) proj[jj] = s;
       }
-    }
+    });
     tids[(r * (1 + g.Te)) * rows + t] = (uint16_t)id;
     uint32_t used = 0;
     for (int tt = 0; tt < g.Te; ++tt) {

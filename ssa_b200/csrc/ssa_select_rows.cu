@@ -201,31 +201,17 @@ __device__ __forceinline__ uint32_t warp_sort_desc(uint32_t v) {
   return v;
 }
 
-// The kth largest (1-based) order key among the participants of ok[0..n):
-// entries whose order key is >= lo (all entries if fewer than kth qualify).
-// Each round histograms the participants of the current key range [ulo, uhi]
-// into 256 bins of width 2^s (s the smallest shift that fits the range) and
-// narrows the range to the bin that holds the kth; once that bin has at most
-// 32 entries they are sorted across the warp. Returns the key T and, in
-// *need, how many entries equal to T belong to the top kth. `list` holds 32
-// entries. Warp-collective.
-__device__ uint32_t warp_select_kth(const uint32_t* ok, int n, int kth, uint32_t lo, uint32_t* hist,
-                                    uint32_t* list, int* need_out) {
+// Narrows [ulo, uhi] -- an order-key range of ok[0..n) holding the entry of
+// rank `need` (1-based, from the top) among the entries inside the range --
+// by rounds of 256-bin histograms of the entries in the range (bin width 2^s,
+// s the smallest shift that fits it), keeping the bin that holds that rank and
+// updating `need` to the rank within it. Stops when the range is a single key
+// (returns 0) or its bin holds at most 32 entries (returns their count).
+// Warp-collective.
+__device__ int warp_narrow_kth(const uint32_t* ok, int n, uint32_t& ulo, uint32_t& uhi, int& need,
+                               uint32_t* hist) {
   const int lane = threadIdx.x & 31;
-  uint32_t mx = 0u, mn = 0xFFFFFFFFu, cntp = 0u;
-  for (int i = lane; i < n; i += 32) {
-    const uint32_t u = ok[i];
-    if (u >= lo) { mx = max(mx, u); mn = min(mn, u); ++cntp; }
-  }
-  if ((int)__reduce_add_sync(0xffffffffu, cntp) < kth) {
-    mx = 0u; mn = 0xFFFFFFFFu;
-    for (int i = lane; i < n; i += 32) { const uint32_t u = ok[i]; mx = max(mx, u); mn = min(mn, u); }
-  }
-  uint32_t uhi = __reduce_max_sync(0xffffffffu, mx);
-  uint32_t ulo = __reduce_min_sync(0xffffffffu, mn);
-  int need = kth;
-  while (true) {
-    if (ulo == uhi) break;
+  while (ulo != uhi) {
     const uint32_t span1 = uhi - ulo;  // span - 1
     const int bl = 32 - __clz(span1);
     const int sh = bl > 8 ? bl - 8 : 0;
@@ -273,31 +259,38 @@ __device__ uint32_t warp_select_kth(const uint32_t* ok, int n, int kth, uint32_t
     ulo = nlo;
     uhi = nhi;
     __syncwarp();
-    if (ulo != uhi && cb <= 32u) {
-      int k = 0;
-      for (int i0 = 0; i0 < n; i0 += 32) {
-        const int i = i0 + lane;
-        uint32_t u = 0u;
-        bool m = false;
-        if (i < n) {
-          u = ok[i];
-          m = u >= ulo && u <= uhi;
-        }
-        const unsigned bm = __ballot_sync(0xffffffffu, m);
-        if (m) list[k + __popc(bm & ((1u << lane) - 1u))] = u;
-        k += __popc(bm);
-      }
-      __syncwarp();
-      const uint32_t v = warp_sort_desc((uint32_t)lane < cb ? list[lane] : 0u);
-      const uint32_t T = __shfl_sync(0xffffffffu, v, need - 1);
-      const int gt = __popc(__ballot_sync(0xffffffffu, (uint32_t)lane < cb && v > T));
-      __syncwarp();
-      *need_out = need - gt;
-      return T;
-    }
+    if (ulo != uhi && cb <= 32u) return (int)cb;
   }
-  *need_out = need;
-  return ulo;
+  return 0;
+}
+
+// The key T of rank `need` among the cb (<= 32) entries of ok[0..n) inside
+// [ulo, uhi], found by sorting them across the warp; *need_out = how many
+// entries equal to T belong to the selection. `list` holds 32 entries.
+// Warp-collective.
+__device__ uint32_t warp_kth_in_bin(const uint32_t* ok, int n, uint32_t ulo, uint32_t uhi, int need, int cb,
+                                    uint32_t* list, int* need_out) {
+  const int lane = threadIdx.x & 31;
+  int k = 0;
+  for (int i0 = 0; i0 < n; i0 += 32) {
+    const int i = i0 + lane;
+    uint32_t u = 0u;
+    bool m = false;
+    if (i < n) {
+      u = ok[i];
+      m = u >= ulo && u <= uhi;
+    }
+    const unsigned bm = __ballot_sync(0xffffffffu, m);
+    if (m) list[k + __popc(bm & ((1u << lane) - 1u))] = u;
+    k += __popc(bm);
+  }
+  __syncwarp();
+  const uint32_t v = warp_sort_desc(lane < cb ? list[lane] : 0u);
+  const uint32_t T = __shfl_sync(0xffffffffu, v, need - 1);
+  const int gt = __popc(__ballot_sync(0xffffffffu, lane < cb && v > T));
+  __syncwarp();
+  *need_out = need - gt;
+  return T;
 }
 
 struct RowsSmem {
@@ -358,10 +351,12 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
   const int64_t total = (int64_t)g.B * g.H * g.N;
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; row < total; row += nwarps) {
-    const int n = (int)(row % g.N);  // row within q and the outputs
+    // 32-bit division: the tensor-core path has fewer than 2^31 rows.
+    const uint32_t bh32 = (uint32_t)row / (uint32_t)g.N;
+    const int n = (int)((uint32_t)row - bh32 * (uint32_t)g.N);  // row within q and the outputs
     const int na = g.row0 + n;        // its sequence position (causal limit, window, self)
-    const int64_t bh = row / g.N;
-    const int b = (int)(bh / g.H), h = (int)(bh % g.H);
+    const int64_t bh = bh32;
+    const int b = (int)(bh32 / (uint32_t)g.H), h = (int)(bh32 - (uint32_t)b * (uint32_t)g.H);
     const int gk = h / g.rep;
     const int bg = b * g.n_kv + gk;
     // Two scan groups (even / odd key tiles) each fill half of the buffer.
@@ -400,10 +395,38 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
       continue;
     }
     const int c = cnt_all;
-    for (int i = lane; i < c; i += 32) {
-      const unsigned long long e = __ldcs(bo + (i < cnt0 ? i : half_cap + i - cnt0));  // read once
-      S.ok[i] = okey(__uint_as_float((uint32_t)e));
-      S.ky[i] = (uint16_t)(e >> 32);
+    // The select's starting range is gathered on the way: the order keys at or
+    // above lo = okey(tau) (count, min, max) and the min / max of all of them.
+    const uint32_t lo = tau > -INFINITY ? okey(tau == 0.f ? -0.f : tau) : 0u;
+    uint32_t mn1 = 0xFFFFFFFFu, mx1 = 0u, c1 = 0u, mn0 = 0xFFFFFFFFu, mx0 = 0u;
+    auto note_key = [&](uint32_t u) {
+      mn0 = min(mn0, u);
+      mx0 = max(mx0, u);
+      if (u >= lo) {
+        mn1 = min(mn1, u);
+        mx1 = max(mx1, u);
+        ++c1;
+      }
+    };
+    // Two entries per 16-byte load (each half starts 16-byte aligned; an odd
+    // count's last load also reads the unused slot after it, inside the half).
+    for (int hf = 0; hf < 2; ++hf) {
+      const int ch = hf ? cnt1 : cnt0;
+      const ulonglong2* src = reinterpret_cast<const ulonglong2*>(bo + (hf ? half_cap : 0));
+      const int base = hf ? cnt0 : 0;
+      for (int pi = lane; 2 * pi < ch; pi += 32) {
+        const ulonglong2 e2 = __ldcs(src + pi);  // read once
+        const uint32_t u0 = okey(__uint_as_float((uint32_t)e2.x));
+        S.ok[base + 2 * pi] = u0;
+        S.ky[base + 2 * pi] = (uint16_t)(e2.x >> 32);
+        note_key(u0);
+        if (2 * pi + 1 < ch) {
+          const uint32_t u1 = okey(__uint_as_float((uint32_t)e2.y));
+          S.ok[base + 2 * pi + 1] = u1;
+          S.ky[base + 2 * pi + 1] = (uint16_t)(e2.y >> 32);
+          note_key(u1);
+        }
+      }
     }
     // Special keys: pad keys perm_r[M-1], causal self, empty-bucket fallbacks.
     const bool any_empty = g.qempty[row] != 0;
@@ -547,8 +570,10 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
         acc += __shfl_xor_sync(0xffffffffu, acc, 2);
         acc += __shfl_xor_sync(0xffffffffu, acc, 4);
         if (j < ndot && sub == 0) {
-          S.ok[c + j] = okey(acc);
+          const uint32_t u = okey(acc);
+          S.ok[c + j] = u;
           S.ky[c + j] = (uint16_t)S.spec[32 + j];
+          note_key(u);
         }
       }
     }
@@ -557,35 +582,87 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
 
     // Exact top-A (the whole pool when it has at most A entries). At least A
     // entries reached tau, so the A-th largest is >= tau and only those take
-    // part in the select.
+    // part in the select (all entries if fewer than A did).
     const int n_elig = min(tot, g.A);
     if (tot > g.A) {
-      const float tz = tau == 0.f ? -0.f : tau;
-      const uint32_t lo = tau > -INFINITY ? okey(tz) : 0u;
-      int need;
-      const uint32_t T = warp_select_kth(S.ok, tot, g.A, lo, S.hist, reinterpret_cast<uint32_t*>(S.spec), &need);
-      // Compact the selection to the front: keys > T, then `need` keys == T
-      // in index order (ties are the reference's unspecified topk order).
-      int wpos = 0, eq_seen = 0;
-      for (int i0 = 0; i0 < tot; i0 += 32) {
-        const int i = i0 + lane;
-        const bool in = i < tot;
-        const uint32_t u = in ? S.ok[i] : 0u;
-        const uint16_t kv = in ? S.ky[i] : 0;
-        const bool eq = in && u == T;
-        const unsigned eqm = __ballot_sync(0xffffffffu, eq);
-        const int eq_rank = eq_seen + __popc(eqm & ((1u << lane) - 1u));
-        const bool sel = in && (u > T || (eq && eq_rank < need));
+      const bool above = (int)__reduce_add_sync(0xffffffffu, c1) >= g.A;
+      uint32_t ulo = __reduce_min_sync(0xffffffffu, above ? mn1 : mn0);
+      uint32_t uhi = __reduce_max_sync(0xffffffffu, above ? mx1 : mx0);
+      int need = g.A;
+      const int cb = warp_narrow_kth(S.ok, tot, ulo, uhi, need, S.hist);
+      uint32_t* list_u = reinterpret_cast<uint32_t*>(S.spec);  // [32]; the special keys are done
+      int wpos = 0;
+      if (mode == 0 && cb > 0) {
+        // One pass: entries above the bin go to the front; the bin's cb
+        // entries are collected (index order), sorted to find the rank-`need`
+        // key T, and the selected ones follow: those above T, then the first
+        // entries equal to T.
+        uint16_t* list_k = reinterpret_cast<uint16_t*>(S.spec + 32);
+        int lc = 0;
+        for (int i0 = 0; i0 < tot; i0 += 32) {
+          const int i = i0 + lane;
+          const bool in = i < tot;
+          const uint32_t u = in ? S.ok[i] : 0u;
+          const uint16_t kv = in ? S.ky[i] : 0;
+          const bool top = in && u > uhi;
+          const bool mid = in && u >= ulo && u <= uhi;
+          const unsigned tm = __ballot_sync(0xffffffffu, top);
+          const unsigned mm = __ballot_sync(0xffffffffu, mid);
+          __syncwarp();
+          if (top) {
+            const int dst = wpos + __popc(tm & ((1u << lane) - 1u));
+            S.ok[dst] = u;
+            S.ky[dst] = kv;
+          }
+          if (mid) {
+            const int li = lc + __popc(mm & ((1u << lane) - 1u));
+            list_u[li] = u;
+            list_k[li] = kv;
+          }
+          __syncwarp();
+          wpos += __popc(tm);
+          lc += __popc(mm);
+        }
+        const bool inl = lane < cb;
+        const uint32_t lu = inl ? list_u[lane] : 0u;
+        const uint32_t v = warp_sort_desc(lu);
+        const uint32_t T = __shfl_sync(0xffffffffu, v, need - 1);
+        const int need_eq = need - __popc(__ballot_sync(0xffffffffu, inl && v > T));
+        const bool eq = inl && lu == T;
+        const int eq_rank = __popc(__ballot_sync(0xffffffffu, eq) & ((1u << lane) - 1u));
+        const bool sel = inl && (lu > T || (eq && eq_rank < need_eq));
         const unsigned sm = __ballot_sync(0xffffffffu, sel);
-        __syncwarp();
         if (sel) {
           const int dst = wpos + __popc(sm & ((1u << lane) - 1u));
-          S.ok[dst] = u;
-          S.ky[dst] = kv;
+          S.ok[dst] = lu;
+          S.ky[dst] = list_k[lane];
         }
-        __syncwarp();
-        wpos += __popc(sm);
-        eq_seen += __popc(eqm);
+      } else {
+        int need_t = need;
+        const uint32_t T = cb > 0 ? warp_kth_in_bin(S.ok, tot, ulo, uhi, need, cb, list_u, &need_t) : ulo;
+        // Compact the selection to the front: keys > T, then `need_t` keys
+        // == T in index order (ties are the reference's unspecified topk order).
+        int eq_seen = 0;
+        for (int i0 = 0; i0 < tot; i0 += 32) {
+          const int i = i0 + lane;
+          const bool in = i < tot;
+          const uint32_t u = in ? S.ok[i] : 0u;
+          const uint16_t kv = in ? S.ky[i] : 0;
+          const bool eq = in && u == T;
+          const unsigned eqm = __ballot_sync(0xffffffffu, eq);
+          const int eq_rank = eq_seen + __popc(eqm & ((1u << lane) - 1u));
+          const bool sel = in && (u > T || (eq && eq_rank < need_t));
+          const unsigned sm = __ballot_sync(0xffffffffu, sel);
+          __syncwarp();
+          if (sel) {
+            const int dst = wpos + __popc(sm & ((1u << lane) - 1u));
+            S.ok[dst] = u;
+            S.ky[dst] = kv;
+          }
+          __syncwarp();
+          wpos += __popc(sm);
+          eq_seen += __popc(eqm);
+        }
       }
     }
     __syncwarp();
@@ -643,9 +720,11 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
       whi = min(max(g.causal ? na : na + g.window, 0), g.M - 1);
       nwin = whi - wlo + 1 - ((drop_self && na >= wlo && na <= whi) ? 1 : 0);
     }
+    int xhi = -1;  // largest key this lane marked
     auto mark = [&](int x) {
       if (x >= wlo && x <= whi) return;  // window key (or self inside it)
       if (drop_self && x == na) return;
+      xhi = max(xhi, x);
       const uint32_t old = atomicOr(&S.bits[x >> 5], 1u << (x & 31));
       if (old == 0u) atomicOr(&S.l1[x >> 10], 1u << ((x >> 5) & 31));
     };
@@ -653,11 +732,15 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
     for (int j = lane; j < g.G; j += 32) mark(min(max(g.glob[j], 0), g.M - 1));
     if (add_zero && lane == 0) mark(0);
     __syncwarp();
-    // Lane L owns bitmap words [L*wpl, (L+1)*wpl) and visits the nonzero
-    // ones through the summary words: count its keys (and those below wlo),
-    // exclusive-scan across lanes, then emit.
-    const int wpl = (Mw + 31) / 32;
-    const int w0 = min(lane * wpl, Mw), w1 = min(w0 + wpl, Mw);
+    // Lane L owns bitmap words [L*wpl, (L+1)*wpl) of the words in use (up to
+    // the largest marked key: under causal masking a row's keys lie below
+    // its position, so the lanes share that prefix evenly) and visits the
+    // nonzero ones through the summary words: count its keys (and those
+    // below wlo), exclusive-scan across lanes, then emit.
+    const int xmax = __reduce_max_sync(0xffffffffu, xhi);
+    const int Mu = xmax >= 0 ? (xmax >> 5) + 1 : 0;
+    const int wpl = (Mu + 31) / 32;
+    const int w0 = min(lane * wpl, Mu), w1 = min(w0 + wpl, Mu);
     auto lane_words = [&](int l) -> uint32_t {
       uint32_t m1 = S.l1[l];
       const int lb = l * 32;

@@ -534,6 +534,7 @@ static bool make_map(CUtensorMap* m, const void* base, int d, int heads, int row
 bool select_tc_supported(const GraphDev& g) {
   if (g.dtype != kDtBF16 || (g.d != 64 && g.d != 128)) return false;
   if (g.M > 65536 || g.A > 1024) return false;
+  if ((int64_t)g.B * g.H * g.N >= (int64_t(1) << 31)) return false;  // 32-bit row indices in k_rows
   if (g.R + 2 + (g.G < g.C ? g.G : g.C) > 32) return false;  // one special key per lane
   // TMA: 16-byte aligned strides (the base pointers are checked at launch)
   auto al = [](int64_t s) { return (s * 2) % 16 == 0; };
