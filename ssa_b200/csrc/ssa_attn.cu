@@ -227,9 +227,12 @@ __device__ __forceinline__ unsigned long long raw_pair(const RawSlice<DT, EPL>& 
   }
 }
 
+// Occupancy over rows in flight: for bf16 d = 128, 2 rows per 8-lane group at
+// 4 blocks (32 warps) per SM measured 5.90 ms at c2, against 6.25 ms for 4
+// rows at 3 blocks (the gathers hit L2; more warps hide their latency better).
 template <int DT, int EPL, bool FP32W, typename IT>
-__global__ void __launch_bounds__(256, (EPL >= 16 ? (DT == kDtF32 ? 2 : 3) : 4)) k_attn_fwd_v16(AttnDev a) {
-  constexpr int U = 4;  // rows in flight per 8-lane group
+__global__ void __launch_bounds__(256, (EPL >= 16 ? (DT == kDtF32 ? 2 : 4) : 4)) k_attn_fwd_v16(AttnDev a) {
+  constexpr int U = (EPL >= 16 && DT != kDtF32) ? 2 : 4;  // rows in flight per 8-lane group
   extern __shared__ __align__(16) float s_all[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t i = (int64_t)blockIdx.x * 8 + warp;
