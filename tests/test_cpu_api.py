@@ -194,3 +194,49 @@ def test_graph_width_matches_oracle_formula():
         p = _params(K=K, window=w, G=G, A=A, is_cross=cross)
         kall = (0 if cross else 2 * w + 1) + G + A
         assert L.ssa_graph_width(ctypes.byref(p)) == O.lib().ora_merge_width(K, kall, cross)
+
+
+# --- host-side contract of the reference's modules (no device needed) -------
+# The reference's asserts and guards fire before any kernel runs, so they are
+# checked here on CPU: tests/test_gqa_mqa.py:25-66 and
+# tests/test_global_tokens_and_mask_guard.py:51-65 of the reference.
+
+def _small(**kw):
+    base = dict(d_model=64, num_heads=4, num_neighbors=16, window_size=4, num_global_tokens=2,
+                max_num_hashes=3)
+    base.update(kw)
+    return SSAConfig(**base)
+
+
+def test_kv_parameter_counts_scale_with_kv_heads():
+    def kv_params(n_kv):
+        attn = SparseAttention(_small(num_kv_heads=n_kv))
+        return sum(p.numel() for p in attn.Wk.parameters()) + sum(p.numel() for p in attn.Wv.parameters())
+    p1, p2, p4 = kv_params(1), kv_params(2), kv_params(4)
+    assert p1 * 4 == p4 and p2 * 2 == p4 and p1 < p2 < p4
+
+
+@pytest.mark.parametrize("kw", [dict(num_heads=5, num_kv_heads=2),   # heads % kv heads
+                                dict(d_model=60, num_heads=8),       # d_model % heads
+                                dict(max_num_hashes=13),             # at most 12 hyperplanes
+                                dict(lsh_num_probes=-1)])            # probes >= 0
+def test_config_asserts(kw):
+    with pytest.raises(AssertionError):
+        SparseAttention(_small(**kw))
+
+
+def test_reuse_every_must_be_positive():
+    with pytest.raises(AssertionError):
+        CachedGraphSparseTransformer(_small(), num_layers=2, reuse_every=0)
+
+
+def test_attention_mask_raises_before_any_kernel():
+    attn = SparseAttention(_small())
+    with pytest.raises(ValueError, match="attention_mask"):
+        attn(torch.randn(2, 32, 64), attention_mask=torch.ones(2, 32))
+
+
+def test_budget_warning_when_window_and_globals_exceed_k():
+    with pytest.warns(UserWarning, match="budget"):
+        attn = SparseAttention(_small(num_neighbors=8, window_size=4))
+    assert attn.lsh_k == 8  # floored, as the reference does
