@@ -1,8 +1,9 @@
 """Generate the golden fixtures by running the reference implementation.
 
-Run in the build container only (the reference is not present on GPU boxes):
+Run where a checkout of the reference project is present (GPU boxes have
+none), pointing at it with --ref or the SSA_REFERENCE environment variable:
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <reference checkout>
 
 It imports the reference module unmodified and applies the two harness
 canonicalisations the parity contract uses:
@@ -182,9 +183,12 @@ def module_init_fixture(sa):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("SSA_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("SSA_REFERENCE"),
+                    help="directory holding the reference's sparse_attention.py")
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give the reference checkout with --ref or SSA_REFERENCE")
     sys.path.insert(0, args.ref)
     import sparse_attention as sa  # the reference, unmodified
     torch.set_num_threads(os.cpu_count() or 1)
