@@ -241,6 +241,14 @@ class _Job:
                 for qs, ks, vs, nb, valid in graphs]
 
 
+def workload_config(w, parallelism: str) -> dict:
+    """The `config` object of the JSON line, the same for both arms."""
+    return {"workload": w.name, "B": w.B, "N": w.N, "M": w.M, "H": w.H, "n_kv": w.n_kv,
+            "d_head": w.d, "K": w.K, "window": w.window, "R": w.R, "probes": w.T,
+            "causal": w.causal, "cross": w.cross, "parallelism": parallelism,
+            "l2": "flushed (256 MB write) between timed steps"}
+
+
 def run_gpu(args):
     import torch
     import torch.distributed as dist
@@ -348,10 +356,7 @@ def run_gpu(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": w.dtype,
             "data": "synthetic (seeded N(0,1) activations; random-init weights in reference order)",
-            "config": {"workload": w.name, "B": w.B, "N": w.N, "M": w.M, "H": w.H, "n_kv": w.n_kv,
-                       "d_head": w.d, "K": w.K, "window": w.window, "R": w.R, "probes": w.T,
-                       "causal": w.causal, "cross": w.cross, "parallelism": par,
-                       "l2": "flushed (256 MB write) between timed steps"},
+            "config": workload_config(w, par),
             "roofline": {"kernel": "k_attn_fwd", "bound": "hbm", "achieved": attn_gbs, "peak": peak,
                          "unit": "GB/s", "frac": attn_gbs / peak, "traffic": traffic,
                          "peak_source": f"{peak_src} hbm_gbs",
@@ -507,8 +512,8 @@ def run_reference(args):
     res = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": full * 1e3,
            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": w.dtype,
-           "data": "synthetic", "config": {"workload": w.name, "B": w.B, "N": w.N, "H": w.H,
-                                           "n_kv": w.n_kv, "K": w.K},
+           "data": "synthetic", "config": workload_config(
+               w, f"reference arm: the CPU oracle port on {cores} host threads, rank 0 only"),
            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                             "sample": desc},
            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
