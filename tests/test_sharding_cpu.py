@@ -1,7 +1,7 @@
 """Host logic of the multi-GPU partitioning (ssa_b200.sharding), on CPU.
 
 The partition helpers are checked directly. The sharded runners then run
-as two gloo ranks (world_size 2), with the oracle injected as the per-slice
+as gloo ranks (world_size 2, 3 and 4), with the oracle injected as the per-slice
 compute. Their assembled outputs must equal the oracle run on the whole
 problem. The oracle is the checker here: the runners' own compute is the
 CUDA ops, which the GPU tests cover.
@@ -114,10 +114,11 @@ def _worker(rank, world, port, mode, causal, result_path):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode,causal", [("rows", True), ("rows", False), ("groups", True)])
-def test_sharded_runners_match_unsharded(tmp_path, mode, causal):
+@pytest.mark.parametrize("mode,causal,world", [("rows", True, 2), ("rows", False, 2), ("groups", True, 2),
+                                               ("rows", True, 4), ("groups", False, 3)])
+def test_sharded_runners_match_unsharded(tmp_path, mode, causal, world):
     result = str(tmp_path / "out.pt")
-    mp.spawn(_worker, args=(2, _free_port(), mode, causal, result), nprocs=2, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), mode, causal, result), nprocs=world, join=True)
     q, k, v, planes = _problem()
     graph, attn = _oracle_fns(planes)
     nb, valid = graph(q, k, q.shape[2], causal, False, 0)
