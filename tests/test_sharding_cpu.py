@@ -125,3 +125,41 @@ def test_sharded_runners_match_unsharded(tmp_path, mode, causal, world):
     ref = attn(q, k, v, nb, valid)
     out = torch.load(result)
     assert torch.equal(out, ref)
+
+
+def _leaving_worker(rank, world, port, result_path):
+    """Rank 1 leaves before the step's K/V all-gather (between steps, with
+    nothing in flight); rank 0 must get an error from the collective within
+    the process group's timeout rather than wait for ever."""
+    import datetime
+    import time
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    q, k, v, planes = _problem()
+    N = q.shape[2]
+    runner = RowSharded(None, N, world, rank, causal=True, graph_fn=None, attn_fn=None)
+    r0, r1 = runner.rows
+    k_seq = k.permute(2, 0, 1, 3)[r0:r1].contiguous()
+    v_seq = v.permute(2, 0, 1, 3)[r0:r1].contiguous()
+    if rank == 1:
+        dist.destroy_process_group()
+        return
+    t0 = time.monotonic()
+    outcome = "completed"
+    try:
+        runner.gather_kv(k_seq, v_seq)
+    except Exception as e:  # gloo reports the missing peer as a RuntimeError
+        outcome = f"raised {type(e).__name__}"
+    with open(result_path, "w") as f:
+        f.write(f"{outcome} {time.monotonic() - t0:.1f}")
+
+
+def test_rank_leaving_surfaces_as_error_not_hang(tmp_path):
+    result = str(tmp_path / "outcome.txt")
+    mp.spawn(_leaving_worker, args=(2, _free_port(), result), nprocs=2, join=True)
+    outcome, seconds = open(result).read().rsplit(" ", 1)
+    print("surviving rank:", outcome, seconds, "s")
+    assert outcome.startswith("raised"), outcome
+    assert float(seconds) < 60.0
