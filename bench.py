@@ -9,10 +9,11 @@ heads, d=128, K=128, bf16).
 
 One step = SparseAttention's graph build (hash, buckets, candidate scan +
 top-k, merge) and gather attention over q/k/v already resident in HBM.
-Under torchrun each rank runs its own full batch of the workload (weak
-scaling: the path has no cross-rank exchange for this sharding); the step
-time is the maximum over ranks. L2 is flushed (a 256 MB write) between timed
-steps; every step is timed with CUDA events on the launching stream.
+Under torchrun the ranks split ONE job (strong scaling): (batch, kv-head)
+groups with no collective, or query rows with one NCCL all-gather of K/V for
+the long-context config; the step time is the maximum over ranks. L2 is
+flushed (a 256 MB write) between timed steps; every step is timed with CUDA
+events on the launching stream.
 
 Prints one JSON line (rank 0).
 """
@@ -57,6 +58,10 @@ def parse_args(argv=None):
                     help="multi-GPU partitioning (auto: query rows for c3, (batch, kv-head) groups otherwise)")
     ap.add_argument("--baseline-slices", type=int, default=2,
                     help="(batch, kv-group) slices in the CPU baseline sample")
+    ap.add_argument("--no-long-context", action="store_true",
+                    help="skip the second measurement of the long-context config c3 on the same GPUs")
+    ap.add_argument("--no-graph-profile", action="store_true",
+                    help="skip the per-stage timing of the graph build after the timed steps")
     return ap.parse_args(argv)
 
 
@@ -66,6 +71,18 @@ def hbm_peak():
             return float(json.load(f)["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def peaks():
+    """hbm_gbs and bf16_tflops_sustained: MEASURED_PEAKS.json, else the pool's
+    fallback figures."""
+    try:
+        with open(PEAKS_FILE) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops_sustained": float(d["bf16_tflops_sustained"]),
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 class ClockSampler:
@@ -241,12 +258,124 @@ class _Job:
                 for qs, ks, vs, nb, valid in graphs]
 
 
-def workload_config(w, parallelism: str) -> dict:
-    """The `config` object of the JSON line, the same for both arms."""
+def workload_config(w) -> dict:
+    """The `config` object of the JSON line: the workload alone, identical for
+    both arms (how each arm runs it goes in top-level keys)."""
     return {"workload": w.name, "B": w.B, "N": w.N, "M": w.M, "H": w.H, "n_kv": w.n_kv,
             "d_head": w.d, "K": w.K, "window": w.window, "R": w.R, "probes": w.T,
-            "causal": w.causal, "cross": w.cross, "parallelism": parallelism,
-            "l2": "flushed (256 MB write) between timed steps"}
+            "causal": w.causal, "cross": w.cross}
+
+
+def sample_stride(w, A: int) -> int:
+    """Key-tile stride of the sample scan: the library's rule
+    (graph_workspace_layout in ssa_graph.cu), restated for the FLOP count."""
+    capg = ((6 * A + 64) + 7) // 8 * 8
+    fit = capg * 8 // 272
+    tiles = (w.M + 127) // 128
+    s = max(A // 12, 1)
+    if fit > 0 and -(-tiles // s) > fit:
+        s = -(-tiles // fit)
+    return s
+
+
+def scan_flops(w, A: int):
+    """Tensor-core FLOPs the two scan passes issue: per 128-row query tile,
+    one 128 x 128 x d MMA per key tile visited (causal: tiles up to the
+    tile's last row; the sample pass every s-th of them)."""
+    tiles_all = (w.M + 127) // 128
+    s = sample_stride(w, A)
+    full = sample = 0
+    for n0 in range(0, w.N, 128):
+        n_hi = min(w.N, n0 + 128) - 1
+        nkt = min(tiles_all, (n_hi >> 7) + 1) if (w.causal and not w.cross) else tiles_all
+        full += nkt
+        sample += -(-nkt // s)
+    per = 2 * 128 * 128 * w.d * w.B * w.H
+    return full * per, sample * per
+
+
+def graph_roofline(w, m, stage_ms: dict, ms_graph: float, peaks: dict, traffic: dict):
+    """Per-stage roofline of the graph build: the scans against the sustained
+    bf16 tensor peak, every stage's measured DRAM bytes (ncu, profiles/) over
+    its CUDA-event time against the HBM peak, and the build's compulsory bytes
+    (q and k read, neighbors and valid written) over the whole build."""
+    lsh = m.lsh_builder
+    A = lsh.output_width(w.M, m.lsh_k)
+    s = 4 if w.dtype == "fp32" else 2
+    W = (2 * w.window + 1 if not w.cross else 0) + w.G + A
+    W = min(w.K, W) if w.cross else min(w.K - 1, W) + 1
+    hbm, tflops = peaks["hbm_gbs"], peaks["bf16_tflops_sustained"]
+    out = {"peak_hbm_gbs": hbm, "peak_bf16_tflops_sustained": tflops, "stages": {}}
+    full, sample = scan_flops(w, A)
+    for name, ms in stage_ms.items():
+        st = {"ms": round(ms, 4)}
+        if ms > 0:
+            if name in ("scan_full", "scan_sample") and w.dtype == "bf16":
+                fl = full if name == "scan_full" else sample
+                st.update({"bound": "tensor", "flops": fl, "tflops": fl / (ms / 1e3) / 1e12,
+                           "frac": fl / (ms / 1e3) / 1e12 / tflops})
+            tb = traffic.get(name)
+            if tb:
+                gbs = tb / (ms / 1e3) / 1e9
+                st.update({"dram_bytes": tb, "dram_gbs": gbs, "dram_frac": gbs / hbm})
+        out["stages"][name] = st
+    comp = w.B * w.H * w.N * w.d * s + w.B * w.n_kv * w.M * w.d * s + w.B * w.H * w.N * W * 5
+    out["compulsory_bytes"] = comp
+    out["compulsory_gbs"] = comp / (ms_graph / 1e3) / 1e9
+    out["compulsory_frac"] = out["compulsory_gbs"] / hbm
+    dram = sum(traffic.get(n, 0) for n in stage_ms)
+    out["dram_bytes_measured"] = dram or None
+    return out
+
+
+def time_job(job, stream, flush, steps, warmup, world, dev):
+    """Warm-up, then `steps` timed steps of job (L2 flushed before each);
+    returns the mean (step ms, graph-build ms), each the max over ranks."""
+    import torch
+    import torch.distributed as dist
+    with torch.no_grad():
+        for _ in range(max(warmup, 0)):
+            flush.zero_()
+            job.step(stream, torch.cuda.Event())
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        evs = []
+        for _ in range(steps):
+            flush.zero_()
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record(stream)
+            job.step(stream, e1)
+            e2.record(stream)
+            evs.append((e0, e1, e2))
+        torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(c) for a, b, c in evs)
+    ms_graph = statistics.mean(a.elapsed_time(b) for a, b, c in evs)
+    if world > 1:
+        t = torch.tensor([ms, ms_graph], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ms_graph = [float(x) for x in t.tolist()]
+    return ms, ms_graph
+
+
+def run_long_context(args, dev, flush, world, rank):
+    """The long-context config c3 (B=1, N=32768) on the same GPUs: query-row
+    sharding with the NCCL all-gather of K/V when world > 1, the whole job on
+    one GPU otherwise. Returns its throughput object (rank 0) for the JSON
+    line, so one run of bench.py --gpus N gives both scaling curves."""
+    import torch
+    from ssa_b200.workloads import WORKLOADS, make_module
+    w = WORKLOADS["c3"]
+    plan = "rows" if world > 1 else "single"
+    m = make_module(w, dev)
+    job = _Job(plan, w, m, dev, world, rank)
+    ms, ms_graph = time_job(job, torch.cuda.current_stream(dev), flush, args.steps, args.warmup, world, dev)
+    del job, m
+    return {"workload": "c3", "value": w.B * w.N / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "graph_build_ms": ms_graph, "n_gpus": world, "scaling": "strong",
+            "parallelism": ("query-row sharding: %d rows per GPU, K/V all-gathered (NCCL)" % (w.N // world)
+                            if world > 1 else "one GPU, whole job"),
+            "config": workload_config(w)}
 
 
 def run_gpu(args):
@@ -325,18 +454,40 @@ def run_gpu(args):
     alg_bytes = w.bytes_per_token() * job.tokens_local   # this rank's attention bytes
     attn_gbs = alg_bytes / (ms_attn / 1e3) / 1e9
     step_gbs = w.bytes_per_token() * tokens / (ms / 1e3) / 1e9 / world
-    traffic = None
+    traffic, graph_traffic = None, {}
     try:
         with open(TRAFFIC_FILE) as f:
-            traffic = json.load(f).get(w.name, {}).get("k_attn_fwd") if plan == "single" else None
+            tw = json.load(f).get(w.name, {})
+        if plan == "single" and tw.get("batch") == w.B:
+            traffic = tw.get("k_attn_fwd")
+            graph_traffic = tw.get("graph", {})
     except Exception:
         pass
+
+    # Per-stage times of the graph build: CUDA events the library records at
+    # its stage boundaries (ssa_graph_profile), on extra steps after the timed
+    # ones, L2 flushed before each.
+    stage_ms = None
+    if plan == "single" and not args.no_graph_profile:
+        from ssa_b200 import ops
+        samples = []
+        with torch.no_grad(), ops.graph_profile() as prof:
+            for _ in range(3):
+                flush.zero_()
+                m._graph(job.q, job.k, w.M, job.causal, w.cross)
+                samples.append(prof.times())
+        stage_ms = {k: statistics.median(x[k] for x in samples) for k in samples[0]}
 
     # End to end through the public API with host buffers: pinned q/k/v in,
     # attention output back to pinned host memory, copies inside the timing.
     e2e = None
     if not args.no_e2e and args.mode == "fwd":
         e2e = run_e2e(args, job, dev, flush, world)
+
+    # The long-context config on the same GPUs, as a second object.
+    long_ctx = None
+    if args.workload == "c2" and args.mode == "fwd" and not args.batch and not args.no_long_context:
+        long_ctx = run_long_context(args, dev, flush, world, rank)
 
     result = None
     if rank == 0:
@@ -351,25 +502,39 @@ def run_gpu(args):
                "rows": f"query-row sharding: {w.N // world} rows per GPU, K/V all-gathered (NCCL)"}[plan]
         metric = METRIC if args.mode == "fwd" else \
             "sparse-attn train step (graph + attention fwd + bwd) tokens/s/GPU, one layer's attention core"
+        attn_dram = None
+        if traffic:
+            g_ = traffic / (ms_attn / 1e3) / 1e9
+            attn_dram = {"dram_gbs": g_, "dram_frac": g_ / peak}
         result = {
             "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": w.dtype,
             "data": "synthetic (seeded N(0,1) activations; random-init weights in reference order)",
-            "config": workload_config(w, par),
+            "config": workload_config(w),
+            "parallelism": par,
+            "l2": "flushed (256 MB write) between timed steps",
             "roofline": {"kernel": "k_attn_fwd", "bound": "hbm", "achieved": attn_gbs, "peak": peak,
                          "unit": "GB/s", "frac": attn_gbs / peak, "traffic": traffic,
                          "peak_source": f"{peak_src} hbm_gbs",
-                         "algorithmic_bytes": alg_bytes},
+                         "algorithmic_bytes": alg_bytes,
+                         **(attn_dram or {}),
+                         "note": "achieved counts algorithmic bytes (gathered K/V rows + q + out); the "
+                                 "GQA heads of a kv group re-gather the same rows from L2, so it can "
+                                 "exceed the HBM peak; dram_frac is the measured DRAM traffic"},
             "step_roofline": {"achieved": step_gbs, "frac": step_gbs / peak, "unit": "GB/s",
                               "note": "attention algorithmic bytes over graph build + attention, per GPU"},
+            "graph_roofline": (graph_roofline(w, m, stage_ms, ms_graph, peaks(), graph_traffic)
+                               if stage_ms else None),
             "kernels_ms": {"graph_build": ms_graph, "attention": ms_attn,
                            "graph_build_per_step": [round(x, 3) for x in graph],
+                           **({"graph_stages": {k: round(v, 4) for k, v in stage_ms.items()}} if stage_ms else {}),
                            **({"attention_backward": ms_bwd} if ms_bwd is not None else {})},
             "gpu_launches": launches_all,
             "clocks": clk,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "long_context": long_ctx,
         }
         print(json.dumps(result))
     if world > 1:
@@ -506,14 +671,20 @@ def run_reference(args):
         dt, desc, cores = cpu_sample(w1, m, q, k, v, slices)
         times.append(dt)
     dt = statistics.mean(times)
-    full = dt * (w.B * w.n_kv) / slices
+    factor = (w.B * w.n_kv) / slices
+    full = dt * factor
     value = w.B * w.N / full
     desc = desc.replace(f"{slices} of {w1.B * w1.n_kv}", f"{slices} of {w.B * w.n_kv}")
     res = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
-           "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": full * 1e3,
+           "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": dt * 1e3,
+           "extrapolation": {"factor": factor, "full_job_ms": full * 1e3,
+                             "note": "each step times the sample; value = the whole job's tokens over "
+                                     "the sample time x factor (linear in (batch, kv-group) slices)"},
            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": w.dtype,
-           "data": "synthetic", "config": workload_config(
-               w, f"reference arm: the CPU oracle port on {cores} host threads, rank 0 only"),
+           "data": "synthetic", "config": workload_config(w),
+           "parallelism": f"reference arm: the CPU oracle port on {cores} host threads, rank 0 only",
+           "l2": "n/a (CPU arm)",
            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                             "sample": desc},
            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,

@@ -182,6 +182,27 @@ SSA_API int ssa_attn_bwd(const ssa_attn_params* p, const void* q, const void* k,
                  void* stream);
 
 /*
+ * The inverted neighbor index of a graph (nb, valid) -- every kv head's keys
+ * with the edges (b, h, n, slot) that gathered them, in edge order -- built
+ * once and reused by ssa_attn_bwd_csr for every layer that applies the same
+ * graph: the reference's CachedGraphSparseTransformer shares one graph over
+ * `reuse_every` layers (sparse_attention.py:1741-1792), and ssa_attn_bwd
+ * otherwise rebuilds this index in each layer's backward (the scatter of
+ * index_select's backward, :1149-1150). The index depends only on B, H,
+ * n_kv, N, M, Kn, nb_i64 and the graph. ssa_attn_csr_size gives its bytes;
+ * building needs a workspace of ssa_attn_bwd_workspace_size bytes.
+ * ssa_attn_bwd_csr is ssa_attn_bwd with the index given (same workspace
+ * size; the index is only read).
+ */
+SSA_API size_t ssa_attn_csr_size(const ssa_attn_params* p);
+SSA_API int ssa_attn_build_csr(const ssa_attn_params* p, const void* nb, const uint8_t* valid, void* csr,
+                               size_t csr_bytes, void* workspace, size_t workspace_bytes, void* stream);
+SSA_API int ssa_attn_bwd_csr(const ssa_attn_params* p, const void* q, const void* k, const void* v,
+                             const void* nb, const uint8_t* valid, const void* dO, const float* lse,
+                             void* dq, void* dk, void* dv, const void* csr, size_t csr_bytes,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * ssa_attn_bwd without a workspace argument -- no counterpart in the
  * reference, which allocates through PyTorch. For callers that cannot
  * allocate device memory: a host binding that only receives device buffers
@@ -220,6 +241,15 @@ SSA_API int ssa_neighbor_overlap(const void* nb_a, const uint8_t* valid_a, const
  * ran out (0 = none); synchronises with the device. clear != 0 resets it. */
 SSA_API int32_t ssa_device_error(int32_t clear);
 
+/* Testing aid for that failure path (no counterpart in the reference): the
+ * tensor-core candidate scan's waits on its on-chip barriers give up after
+ * `polls` polls instead of 2^24 (0 restores the default), so a test can make
+ * a wait run out without faulting or hanging the GPU. The kernel then stops
+ * its pipeline, waits for its own copies and MMAs in flight, frees its TMEM
+ * and returns; ssa_device_error reports the code and that build's output is
+ * undefined. Process-wide; read when each build is launched. */
+SSA_API int ssa_debug_set_wait_limit(uint32_t polls);
+
 /* Human-readable text for the last error on this host thread. */
 SSA_API const char* ssa_last_error(void);
 
@@ -227,6 +257,23 @@ SSA_API const char* ssa_last_error(void);
  * host-side count; library calls such as the CUB sort inside ssa_attn_bwd
  * are not included). */
 SSA_API int64_t ssa_kernel_launches(void);
+
+/*
+ * Stage timing of the graph build, for profiling (no counterpart in the
+ * reference). ssa_graph_profile(1) makes every later ssa_build_graph /
+ * ssa_lsh_select call record CUDA events on its stream at the boundaries of
+ * its kernel stages; ssa_graph_profile(0) turns that off. Events are created
+ * on the current device when profiling is turned on.
+ * ssa_graph_stage_times waits for the most recent profiled call to finish and
+ * writes the duration in ms of each of its SSA_GRAPH_STAGES stages, in this
+ * order: key hashing, bucket trim, query hashing, sample scan, threshold
+ * rows, full scan, final rows, FMA scan (exact fallback, or the whole
+ * selection for fp32). A stage the call's path does not run reads 0. The
+ * profiling state is process-wide: profile one call at a time.
+ */
+#define SSA_GRAPH_STAGES 8
+SSA_API int ssa_graph_profile(int32_t enable);
+SSA_API int ssa_graph_stage_times(float* ms_out);
 
 /* ABI version of this library (major * 100 + minor). */
 SSA_API int32_t ssa_abi_version(void);

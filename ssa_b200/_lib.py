@@ -61,14 +61,25 @@ SIGNATURES = {
     "ssa_attn_bwd_workspace_size": (_sz, [ctypes.POINTER(AttnParams)]),
     "ssa_attn_bwd": (ctypes.c_int, [ctypes.POINTER(AttnParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                     _vp, _vp, _vp, _vp, _sz, _vp]),
+    "ssa_attn_csr_size": (_sz, [ctypes.POINTER(AttnParams)]),
+    "ssa_attn_build_csr": (ctypes.c_int, [ctypes.POINTER(AttnParams), _vp, _vp, _vp, _sz, _vp, _sz, _vp]),
+    "ssa_attn_bwd_csr": (ctypes.c_int, [ctypes.POINTER(AttnParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                        _vp, _vp, _vp, _vp, _sz, _vp, _sz, _vp]),
     "ssa_attn_bwd_noalloc": (ctypes.c_int, [ctypes.POINTER(AttnParams), _vp, _vp, _vp, _vp, _vp, _vp,
                                             _vp, _vp, _vp, _vp, _vp]),
     "ssa_neighbor_overlap": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp]),
     "ssa_device_error": (_i32, [_i32]),
+    "ssa_debug_set_wait_limit": (ctypes.c_int, [ctypes.c_uint32]),
     "ssa_last_error": (ctypes.c_char_p, []),
     "ssa_abi_version": (_i32, []),
     "ssa_kernel_launches": (_i64, []),
+    "ssa_graph_profile": (ctypes.c_int, [_i32]),
+    "ssa_graph_stage_times": (ctypes.c_int, [ctypes.POINTER(ctypes.c_float)]),
 }
+
+# ssa_graph_stage_times order (the header's SSA_GRAPH_STAGES stages)
+GRAPH_STAGES = ("hash_keys", "bucket_trim", "hash_queries", "scan_sample", "rows_thresh", "scan_full",
+                "rows_final", "select_fma")
 
 _lib = None
 _lock = threading.Lock()

@@ -473,7 +473,7 @@ class CachedGraphSparseTransformer(nn.Module):
     def forward(self, x, return_stats: bool = False):
         h = x
         stats_list = []
-        cached, cached_group = None, None
+        cached, cached_group, csr = None, None, None
         for i, layer in enumerate(self.layers):
             group = self.group_of[i]
             recompute = group != cached_group
@@ -486,10 +486,11 @@ class CachedGraphSparseTransformer(nn.Module):
             if recompute:
                 cached = self.shared_attn_per_group[group]._graph(q, k, N, attn.config.causal, False)
                 cached_group = group
+                csr = ops.GraphCSR()  # the group's backward passes build its inverted index once
             nb, valid = cached
             drop = ops.new_dropout_key(attn.dp) if (attn.dp > 0.0 and attn.training) else None
             out = ops.gather_attention(q, k, v, nb, valid, attn.scale, attn.config.fp32_attn_weights,
-                                       dropout=drop)
+                                       dropout=drop, csr=csr)
             a = attn.Wo(out.transpose(1, 2).reshape(B, N, attn.H * attn.d_head))
             h = h + a + layer.ff(layer.norm2(h + a))
             if return_stats:

@@ -16,11 +16,12 @@
 // one after another.
 //
 // Backward: per row, dq and the per-edge weights (value weight p, and
-// scale * dS); then the edges are radix-sorted by (kv slice, key) -- a stable
-// sort, so within a key edges keep their row order -- and one warp per key
-// sums its segment in that order into dk/dv. No floating-point atomics: the
-// result is bitwise reproducible.
-#include <cub/device/device_radix_sort.cuh>
+// scale * dS); then the inverted neighbor index -- the edges of each (batch,
+// kv-head) slice stably sorted by key (a hand-written LSD radix sort, so
+// within a key edges keep their row order) -- and the dk/dv sums over each
+// key's sorted segment, in that order. No floating-point atomics: the result
+// is bitwise reproducible. The index depends only on the graph, so layers
+// that share a graph can build it once (ssa_attn_build_csr).
 
 #include "ssa_common.cuh"
 #include "ssa_internal.h"
@@ -412,13 +413,10 @@ __global__ void __launch_bounds__(256) k_attn_bwd_rows(AttnDev a) {
   for (int j = lane; j < a.Kn; j += 32) dsum = fmaf(sp[j], sdp[j], dsum);
 #pragma unroll
   for (int o = 16; o; o >>= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, o);
-  const uint32_t BGM = (uint32_t)(a.B * a.n_kv) * (uint32_t)a.M;
-  const uint32_t bgM = (uint32_t)(b * a.n_kv + g) * (uint32_t)a.M;
   for (int j = lane, kk = 0; j < a.Kn; j += 32, ++kk) {
     const float p = sp[j];
     const float ds = p * (sdp[j] - dsum) * a.scale;
     const int64_t e = row * a.Kn + j;
-    const bool ok = slot_ok<IT>(a, nbr, vr, j);
     float pv = (DT == kDtBF16 && !FP32W) ? round_bf16(p) : p;  // the weight that multiplied v_j
     if (a.drop_thresh) {
       const bool keep = kk < 32 ? ((keep_bits >> kk) & 1u) != 0
@@ -427,8 +425,6 @@ __global__ void __launch_bounds__(256) k_attn_bwd_rows(AttnDev a) {
     }
     a.ep[e] = pv;
     a.eds[e] = ds;
-    a.ekey[e] = ok ? bgM + (uint32_t)load_nb<IT>(nbr, j) : BGM;
-    a.eid[e] = (uint32_t)e;
     sdp[j] = ds;
   }
   __syncwarp();
@@ -552,13 +548,10 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? 2 : 3)) k_attn_bwd_rows_v16(
   for (int j = lane; j < a.Kn; j += 32) dsum = fmaf(sp[j], sdp[j], dsum);
 #pragma unroll
   for (int o = 16; o; o >>= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, o);
-  const uint32_t BGM = (uint32_t)(a.B * a.n_kv) * (uint32_t)a.M;
-  const uint32_t bgM = (uint32_t)(b * a.n_kv + g) * (uint32_t)a.M;
   for (int j = lane, kk = 0; j < a.Kn; j += 32, ++kk) {
     const float p = sp[j];
     const float ds = p * (sdp[j] - dsum) * a.scale;
     const int64_t e = row * a.Kn + j;
-    const int key = sk[j];
     float pv = (DT == kDtBF16 && !FP32W) ? round_bf16(p) : p;  // the weight that multiplied v_j
     if (a.drop_thresh) {
       const bool keep = kk < 32 ? ((keep_bits >> kk) & 1u) != 0
@@ -567,8 +560,6 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? 2 : 3)) k_attn_bwd_rows_v16(
     }
     a.ep[e] = pv;
     a.eds[e] = ds;
-    a.ekey[e] = key >= 0 ? bgM + (uint32_t)key : BGM;
-    a.eid[e] = (uint32_t)e;
     sdp[j] = ds;
   }
   __syncwarp();
@@ -620,13 +611,201 @@ __device__ __forceinline__ int64_t lower_bound_u32(const uint32_t* a, int64_t n,
   return lo;
 }
 
-// First sorted position of every key (and of the sentinel key, the end of
-// the valid edges): one thread per key, a binary search over the sorted keys.
-__global__ void __launch_bounds__(256) k_seg_starts(AttnDev a, int64_t n_edges) {
+// First sorted position of every key, and seg[B*n_kv*M] = the number of
+// valid edges: one thread per key, a binary search over the sorted keys.
+__global__ void __launch_bounds__(256) k_seg_starts(AttnDev a, const uint32_t* n_valid) {
   const int64_t key = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t total = (int64_t)a.B * a.n_kv * a.M;
   if (key > total) return;
-  a.seg[key] = (uint32_t)lower_bound_u32(a.skey, n_edges, (uint32_t)key);
+  a.seg[key] = (uint32_t)lower_bound_u32(a.skey, (int64_t)__ldg(n_valid), (uint32_t)key);
+}
+
+// ---------------------------------------------------------------------------
+// Backward, stage 2: the inverted neighbor index (CSR). The edges (b, h, n,
+// slot) of one (batch, kv-head) slice are contiguous -- rows b*H + h with
+// h / rep = g, i.e. rows rep*bg .. rep*bg + rep - 1 -- so sorting each slice
+// by key, least significant 8-bit digit first, sorts all edges by
+// (slice, key). Invalid slots carry the key M, sorted last in every pass but
+// the final one, which drops them and writes the composite key bg * M + key.
+// Each pass runs over 4096-edge tiles of a slice:
+//   k_esort_hist     256-bin histogram of the tile's digits;
+//   k_esort_scan     per slice, an exclusive scan over (digit, tile);
+//   k_esort_base     (final pass) the slices' output offsets;
+//   k_esort_scatter  ranks the tile's edges digit by digit in edge order --
+//                    each warp takes 512 consecutive edges 32 at a time,
+//                    __match_any_sync groups equal digits, per-warp counters
+//                    give the rank, a scan over warps orders the warps -- so
+//                    the sort is stable, and writes them to their slots.
+// ---------------------------------------------------------------------------
+constexpr int kSortTile = 4096;  // edges per tile: 8 warps x 16 rounds x 32
+
+struct SortPass {
+  const uint32_t* kin;   // keys in; null in the first pass (read from nb / valid)
+  const uint32_t* iin;   // edge ids in; null in the first pass (the edge's position)
+  uint32_t* kout;
+  uint32_t* iout;
+  uint32_t* counts;      // [BG][256][tiles]: counts, then tile offsets
+  uint32_t* totals;      // [BG] edges counted per slice
+  uint32_t* base;        // [BG + 1] final pass: first output slot of each slice; [BG] = all
+  int shift;             // digit = (key >> shift) & 255
+  int final_pass;        // drop invalid edges, write bg * M + key
+  int tiles;             // tiles per slice
+  int64_t slice_edges;   // rep * N * Kn
+};
+
+// Key of edge e: its neighbor index if the slot takes part (valid, inside
+// [0, M)), else M.
+template <typename IT>
+__device__ __forceinline__ uint32_t edge_key(const AttnDev& a, const SortPass& sp, int64_t e) {
+  if (sp.kin) return __ldg(sp.kin + e);
+  if (!__ldg(a.valid + e)) return (uint32_t)a.M;
+  const int64_t x = (int64_t)__ldg(static_cast<const IT*>(a.nb) + e);
+  return (x >= 0 && x < a.M) ? (uint32_t)x : (uint32_t)a.M;
+}
+
+template <typename IT>
+__global__ void __launch_bounds__(256) k_esort_hist(AttnDev a, SortPass sp) {
+  __shared__ uint32_t hist[256];
+  const int t = blockIdx.x, bg = blockIdx.y;
+  const int64_t e0 = bg * sp.slice_edges + (int64_t)t * kSortTile;
+  const int64_t e1 = min(e0 + kSortTile, (bg + 1) * sp.slice_edges);
+  hist[threadIdx.x] = 0;
+  __syncthreads();
+  for (int64_t e = e0 + threadIdx.x; e < e1; e += 256) {
+    const uint32_t key = edge_key<IT>(a, sp, e);
+    if (sp.final_pass && key >= (uint32_t)a.M) continue;
+    atomicAdd(&hist[(key >> sp.shift) & 255u], 1u);
+  }
+  __syncthreads();
+  sp.counts[((int64_t)bg * 256 + threadIdx.x) * sp.tiles + t] = hist[threadIdx.x];
+}
+
+// One block per slice: counts[bg][digit][tile] -> exclusive prefix in
+// (digit, tile) order; totals[bg] = the slice's count.
+__global__ void __launch_bounds__(1024) k_esort_scan(SortPass sp) {
+  __shared__ uint32_t wsum[32];
+  const int bg = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t* c = sp.counts + (int64_t)bg * 256 * sp.tiles;
+  const int n = 256 * sp.tiles;
+  const int per = (n + 1023) / 1024;
+  const int i0 = min(threadIdx.x * per, n), i1 = min(i0 + per, n);
+  uint32_t sum = 0;
+  for (int i = i0; i < i1; ++i) sum += c[i];
+  uint32_t incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = wsum[lane], wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += v;
+    }
+    wsum[lane] = wi - w;  // exclusive prefix of the warp sums
+    if (lane == 31) sp.totals[bg] = wi;
+  }
+  __syncthreads();
+  uint32_t run = wsum[warp] + incl - sum;
+  for (int i = i0; i < i1; ++i) {
+    const uint32_t v = c[i];
+    c[i] = run;
+    run += v;
+  }
+}
+
+// Final pass: base[bg] = edges kept in the slices before bg; base[BG] = all.
+__global__ void __launch_bounds__(1024) k_esort_base(SortPass sp, int BG) {
+  __shared__ uint32_t wsum[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int per = (BG + 1023) / 1024;
+  const int i0 = min((int)threadIdx.x * per, BG), i1 = min(i0 + per, BG);
+  uint32_t sum = 0;
+  for (int i = i0; i < i1; ++i) sum += sp.totals[i];
+  uint32_t incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = wsum[lane], wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += v;
+    }
+    wsum[lane] = wi - w;
+    if (lane == 31) sp.base[BG] = wi;
+  }
+  __syncthreads();
+  uint32_t run = wsum[warp] + incl - sum;
+  for (int i = i0; i < i1; ++i) {
+    sp.base[i] = run;
+    run += sp.totals[i];
+  }
+}
+
+template <typename IT>
+__global__ void __launch_bounds__(256) k_esort_scatter(AttnDev a, SortPass sp) {
+  constexpr int ROUNDS = kSortTile / 256;  // 16 rounds of 32 edges per warp
+  __shared__ uint32_t wcnt[8][257];        // per-warp digit counts, then warp offsets
+  __shared__ uint32_t toff[256];           // first output slot of each digit of this tile
+  const int t = blockIdx.x, bg = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t e0 = bg * sp.slice_edges + (int64_t)t * kSortTile;
+  const int64_t e1 = min(e0 + kSortTile, (bg + 1) * sp.slice_edges);
+  for (int i = threadIdx.x; i < 8 * 257; i += 256) (&wcnt[0][0])[i] = 0;
+  const uint32_t sbase = sp.final_pass ? sp.base[bg] : (uint32_t)(bg * sp.slice_edges);
+  toff[threadIdx.x] = sbase + sp.counts[((int64_t)bg * 256 + threadIdx.x) * sp.tiles + t];
+  __syncthreads();
+  uint32_t key[ROUNDS], id[ROUNDS], rank[ROUNDS];
+  int dig[ROUNDS];
+#pragma unroll
+  for (int r = 0; r < ROUNDS; ++r) {
+    const int64_t e = e0 + warp * (32 * ROUNDS) + r * 32 + lane;
+    const bool in = e < e1;
+    key[r] = in ? edge_key<IT>(a, sp, e) : (uint32_t)a.M;
+    id[r] = in ? (sp.iin ? __ldg(sp.iin + e) : (uint32_t)e) : 0u;
+    const bool live = in && !(sp.final_pass && key[r] >= (uint32_t)a.M);
+    const int d = live ? (int)((key[r] >> sp.shift) & 255u) : 256;  // 256: takes no slot
+    const unsigned peers = __match_any_sync(0xffffffffu, d);
+    const int leader = __ffs(peers) - 1;
+    uint32_t before = 0;
+    if (lane == leader) {
+      before = wcnt[warp][d];
+      wcnt[warp][d] = before + __popc(peers);
+    }
+    before = __shfl_sync(0xffffffffu, before, leader);
+    rank[r] = before + __popc(peers & ((1u << lane) - 1u));
+    dig[r] = live ? d : -1;
+    __syncwarp();
+  }
+  __syncthreads();
+  {  // warp order within each digit
+    const int d = threadIdx.x;
+    uint32_t run = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const uint32_t v = wcnt[w][d];
+      wcnt[w][d] = run;
+      run += v;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < ROUNDS; ++r) {
+    if (dig[r] < 0) continue;
+    const uint32_t pos = toff[dig[r]] + wcnt[warp][dig[r]] + rank[r];
+    sp.kout[pos] = sp.final_pass ? (uint32_t)bg * (uint32_t)a.M + key[r] : key[r];
+    sp.iout[pos] = id[r];
+  }
 }
 
 // dk / dv as a segmented sum over the edges sorted by (kv slice, key). Each
@@ -825,36 +1004,126 @@ cudaError_t launch_attn_fwd(const AttnDev& a, cudaStream_t st) {
   return a.dtype == kDtF32 ? fwd_d<kDtF32>(a, st) : fwd_d<kDtBF16>(a, st);
 }
 
-size_t attn_bwd_workspace_layout(const AttnDev& a, AttnDev* out, void* ws) {
-  const int64_t E = (int64_t)a.B * a.H * a.N * a.Kn;
-  size_t tmp = 0;
-  cub::DeviceRadixSort::SortPairs(nullptr, tmp, (const uint32_t*)nullptr, (uint32_t*)nullptr,
-                                  (const uint32_t*)nullptr, (uint32_t*)nullptr, (int)E, 0, 32);
+// Geometry of the edge sort: E edges; a slice's rep * N * Kn edges in
+// `tiles` tiles; `passes` 8-bit digits cover keys 0..M (M marks invalid).
+struct SortGeom {
+  int64_t E, slice_edges;
+  int tiles, passes, BG;
+};
+
+static SortGeom sort_geom(const AttnDev& a) {
+  SortGeom g;
+  g.E = (int64_t)a.B * a.H * a.N * a.Kn;
+  g.BG = a.B * a.n_kv;
+  g.slice_edges = (int64_t)a.rep * a.N * a.Kn;
+  g.tiles = (int)((g.slice_edges + kSortTile - 1) / kSortTile);
+  const int bits = 32 - __builtin_clz((unsigned)a.M);  // M itself must fit
+  g.passes = (bits + 7) / 8;
+  return g;
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+size_t attn_csr_layout(const AttnDev& a, AttnDev* out, void* csr) {
+  const SortGeom sg = sort_geom(a);
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
-    off = (off + bytes + 255) & ~size_t(255);
+    off = align256(off + bytes);
     return o;
   };
-  const size_t o_ep = take(4 * E), o_eds = take(4 * E), o_ekey = take(4 * E), o_eid = take(4 * E);
-  const size_t o_skey = take(4 * E), o_sid = take(4 * E), o_tmp = take(tmp);
-  const size_t o_seg = take(4 * ((size_t)a.B * a.n_kv * a.M + 1));
+  const size_t o_skey = take(4 * sg.E), o_sid = take(4 * sg.E);
+  const size_t o_seg = take(4 * ((size_t)sg.BG * a.M + 1));
+  if (out) {
+    char* base = static_cast<char*>(csr);
+    out->skey = reinterpret_cast<uint32_t*>(base + o_skey);
+    out->sid = reinterpret_cast<uint32_t*>(base + o_sid);
+    out->seg = reinterpret_cast<uint32_t*>(base + o_seg);
+  }
+  return off;
+}
+
+size_t attn_bwd_workspace_layout(const AttnDev& a, AttnDev* out, void* ws) {
+  const SortGeom sg = sort_geom(a);
+  const int64_t E = sg.E;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  const size_t o_ep = take(4 * E), o_eds = take(4 * E);
+  const size_t o_tk0 = take(4 * E), o_ti0 = take(4 * E);
+  size_t o_tk1 = 0, o_ti1 = 0;
+  if (sg.passes >= 3) {
+    o_tk1 = take(4 * E);
+    o_ti1 = take(4 * E);
+  }
+  const size_t o_cnt = take(4 * (size_t)sg.BG * 256 * sg.tiles);
+  const size_t o_tot = take(4 * (size_t)sg.BG), o_base = take(4 * ((size_t)sg.BG + 1));
   const size_t chunks = (size_t)(E + kDkdvChunk - 1) / kDkdvChunk;
   const size_t o_part = take(sizeof(float) * chunks * 4 * (size_t)a.d);
+  const size_t o_csr = off;
+  off += attn_csr_layout(a, nullptr, nullptr);  // the inverted index, when the call builds its own
   if (out) {
     char* base = static_cast<char*>(ws);
     out->ep = reinterpret_cast<float*>(base + o_ep);
     out->eds = reinterpret_cast<float*>(base + o_eds);
-    out->ekey = reinterpret_cast<uint32_t*>(base + o_ekey);
-    out->eid = reinterpret_cast<uint32_t*>(base + o_eid);
-    out->skey = reinterpret_cast<uint32_t*>(base + o_skey);
-    out->sid = reinterpret_cast<uint32_t*>(base + o_sid);
-    out->sort_tmp = base + o_tmp;
-    out->seg = reinterpret_cast<uint32_t*>(base + o_seg);
+    out->tk0 = reinterpret_cast<uint32_t*>(base + o_tk0);
+    out->ti0 = reinterpret_cast<uint32_t*>(base + o_ti0);
+    out->tk1 = sg.passes >= 3 ? reinterpret_cast<uint32_t*>(base + o_tk1) : nullptr;
+    out->ti1 = sg.passes >= 3 ? reinterpret_cast<uint32_t*>(base + o_ti1) : nullptr;
+    out->cnt = reinterpret_cast<uint32_t*>(base + o_cnt);
+    out->tot = reinterpret_cast<uint32_t*>(base + o_tot);
+    out->sbase = reinterpret_cast<uint32_t*>(base + o_base);
     out->part = reinterpret_cast<float*>(base + o_part);
-    out->sort_tmp_bytes = tmp;
+    attn_csr_layout(a, out, base + o_csr);
   }
   return off;
+}
+
+// The inverted neighbor index into a.skey / a.sid / a.seg: the LSD passes,
+// then every key's segment start.
+template <typename IT>
+static cudaError_t build_csr_t(const AttnDev& a, cudaStream_t st) {
+  const SortGeom sg = sort_geom(a);
+  const dim3 grid(sg.tiles, sg.BG);
+  const uint32_t* kin = nullptr;
+  const uint32_t* iin = nullptr;
+  for (int pass = 0; pass < sg.passes; ++pass) {
+    SortPass sp;
+    sp.kin = kin;
+    sp.iin = iin;
+    sp.final_pass = pass == sg.passes - 1;
+    sp.kout = sp.final_pass ? a.skey : (pass & 1 ? a.tk1 : a.tk0);
+    sp.iout = sp.final_pass ? a.sid : (pass & 1 ? a.ti1 : a.ti0);
+    sp.counts = a.cnt;
+    sp.totals = a.tot;
+    sp.base = a.sbase;
+    sp.shift = 8 * pass;
+    sp.tiles = sg.tiles;
+    sp.slice_edges = sg.slice_edges;
+    k_esort_hist<IT><<<grid, 256, 0, st>>>(a, sp);
+    note_launch();
+    k_esort_scan<<<sg.BG, 1024, 0, st>>>(sp);
+    note_launch();
+    if (sp.final_pass) {
+      k_esort_base<<<1, 1024, 0, st>>>(sp, sg.BG);
+      note_launch();
+    }
+    k_esort_scatter<IT><<<grid, 256, 0, st>>>(a, sp);
+    note_launch();
+    kin = sp.kout;
+    iin = sp.iout;
+  }
+  const int64_t keys = (int64_t)sg.BG * a.M;
+  k_seg_starts<<<(unsigned)((keys + 1 + 255) / 256), 256, 0, st>>>(a, a.sbase + sg.BG);
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_build_csr(const AttnDev& a, cudaStream_t st) {
+  return a.nb_i64 ? build_csr_t<int64_t>(a, st) : build_csr_t<int32_t>(a, st);
 }
 
 template <int DT, int EPL, bool FP32W, typename IT>
@@ -890,24 +1159,16 @@ static cudaError_t bwd_rows_e(const AttnDev& a, cudaStream_t st) {
 }
 
 template <int DT>
-static cudaError_t bwd_d(const AttnDev& a, cudaStream_t st) {
+static cudaError_t bwd_d(const AttnDev& a, bool build_csr, cudaStream_t st) {
   cudaError_t e;
   if (a.d <= 32) e = bwd_rows_e<DT, 4>(a, st);
   else if (a.d <= 64) e = bwd_rows_e<DT, 8>(a, st);
   else if (a.d <= 128) e = bwd_rows_e<DT, 16>(a, st);
   else e = bwd_rows_e<DT, 32>(a, st);
   if (e != cudaSuccess) return e;
+  if (build_csr && (e = launch_build_csr(a, st)) != cudaSuccess) return e;
   const int64_t E = (int64_t)a.B * a.H * a.N * a.Kn;
-  const uint64_t maxkey = (uint64_t)a.B * a.n_kv * a.M;
-  int end_bit = 1;
-  while ((1ull << end_bit) <= maxkey) ++end_bit;
-  size_t tmp = a.sort_tmp_bytes;
-  e = cub::DeviceRadixSort::SortPairs(a.sort_tmp, tmp, a.ekey, a.skey, a.eid, a.sid, (int)E, 0,
-                                      end_bit, st);
-  if (e != cudaSuccess) return e;
   const int64_t keys = (int64_t)a.B * a.n_kv * a.M;
-  k_seg_starts<<<(unsigned)((keys + 1 + 255) / 256), 256, 0, st>>>(a, E);
-  note_launch();
   const int64_t chunks = (E + kDkdvChunk - 1) / kDkdvChunk;
   const unsigned grid = (unsigned)((chunks + 7) / 8);
   if (chunks > 0) {
@@ -926,8 +1187,8 @@ static cudaError_t bwd_d(const AttnDev& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_attn_bwd(const AttnDev& a, cudaStream_t st) {
-  return a.dtype == kDtF32 ? bwd_d<kDtF32>(a, st) : bwd_d<kDtBF16>(a, st);
+cudaError_t launch_attn_bwd(const AttnDev& a, bool build_csr, cudaStream_t st) {
+  return a.dtype == kDtF32 ? bwd_d<kDtF32>(a, build_csr, st) : bwd_d<kDtBF16>(a, build_csr, st);
 }
 
 }  // namespace ssa

@@ -79,9 +79,15 @@ int check_graph(const ssa_graph_params* p) {
   return SSA_OK;
 }
 
+// Polls before a tensor-core scan wait gives up (ssa_debug_set_wait_limit);
+// 0: the default, 2^24.
+std::atomic<uint32_t> g_wait_limit{0};
+
 ssa::GraphDev dev_of(const ssa_graph_params* p) {
   ssa::GraphDev g;
   memset(&g, 0, sizeof(g));
+  const uint32_t wl = g_wait_limit.load(std::memory_order_relaxed);
+  g.wait_limit = wl ? wl : (1u << 24);
   g.B = p->B; g.H = p->H; g.n_kv = p->n_kv; g.rep = p->H / p->n_kv; g.N = p->N; g.M = p->M;
   g.d = p->d; g.dtype = p->dtype; g.R = p->R; g.max_p = p->max_p; g.p = p->p_eff; g.C = p->C;
   g.Te = p->T < p->p_eff ? p->T : p->p_eff;
@@ -122,15 +128,31 @@ int check_select_fits(const ssa::GraphDev& g) {
 namespace ssa {
 static std::atomic<long long> g_kernel_launches{0};
 void note_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
+
+// Graph-build stage profiling: one set of events per process, recorded by
+// every build while enabled (the device of the enabling call).
+static std::mutex g_prof_mu;
+static bool g_prof_on = false;
+static cudaEvent_t g_prof_ev[kStageMarks] = {};
+
+void stage_mark(int i, cudaStream_t st) {
+  if (!g_prof_on) return;
+  cudaEventRecord(g_prof_ev[i], st);
+}
 }  // namespace ssa
 
 extern "C" {
 
 const char* ssa_last_error(void) { return g_err; }
 
-int32_t ssa_abi_version(void) { return 104; }
+int32_t ssa_abi_version(void) { return 105; }
 
 int32_t ssa_device_error(int32_t clear) { return ssa::read_device_error(clear); }
+
+int ssa_debug_set_wait_limit(uint32_t polls) {
+  g_wait_limit.store(polls, std::memory_order_relaxed);
+  return SSA_OK;
+}
 
 int32_t ssa_graph_width(const ssa_graph_params* p) { return p ? graph_width(p) : -1; }
 
@@ -266,6 +288,14 @@ int ssa_attn_fwd(const ssa_attn_params* p, const void* q, const void* k, const v
   return SSA_OK;
 }
 
+static int check_edges(const ssa_attn_params* p) {
+  const int64_t E = (int64_t)p->B * p->H * p->N * p->Kn;
+  if (E >= (int64_t(1) << 31)) return fail(SSA_ERR_UNSUPPORTED, "too many edges (%lld)", (long long)E);
+  if ((int64_t)p->B * p->n_kv * p->M >= (int64_t(1) << 31))
+    return fail(SSA_ERR_UNSUPPORTED, "B * n_kv * M too large");
+  return SSA_OK;
+}
+
 size_t ssa_attn_bwd_workspace_size(const ssa_attn_params* p) {
   if (!p || p->B < 1 || p->H < 1 || p->N < 1 || p->Kn < 1) return 0;
   ssa::AttnDev a = attn_dev(p);
@@ -280,10 +310,7 @@ int ssa_attn_bwd(const ssa_attn_params* p, const void* q, const void* k, const v
   if ((rc = check_rows("dO", dO, p->dtype, p->d, p->o_sb, p->o_sh, p->o_sn))) return rc;
   if ((rc = check_rows("dq", dq, p->dtype, p->d, p->o_sb, p->o_sh, p->o_sn))) return rc;
   if (!lse || !dk || !dv) return fail(SSA_ERR_INVALID, "lse/dk/dv are NULL");
-  const int64_t E = (int64_t)p->B * p->H * p->N * p->Kn;
-  if (E >= (int64_t(1) << 31)) return fail(SSA_ERR_UNSUPPORTED, "too many edges (%lld)", (long long)E);
-  if ((int64_t)p->B * p->n_kv * p->M >= (int64_t(1) << 31))
-    return fail(SSA_ERR_UNSUPPORTED, "B * n_kv * M too large");
+  if ((rc = check_edges(p))) return rc;
   ssa::AttnDev a = attn_dev(p);
   const size_t need = ssa::attn_bwd_workspace_layout(a, nullptr, nullptr);
   if (!workspace || workspace_bytes < need)
@@ -291,15 +318,70 @@ int ssa_attn_bwd(const ssa_attn_params* p, const void* q, const void* k, const v
   ssa::attn_bwd_workspace_layout(a, &a, workspace);
   a.q = q; a.k = k; a.v = v; a.nb = nb; a.valid = valid; a.dO = dO; a.lse_in = lse;
   a.dq = dq; a.dk = dk; a.dv = dv;
-  cudaError_t e = ssa::launch_attn_bwd(a, static_cast<cudaStream_t>(stream));
+  cudaError_t e = ssa::launch_attn_bwd(a, true, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attention backward launch");
   return SSA_OK;
 }
 
-// ---------------------------------------------------------------------------
-// Attention backward without a caller workspace: the scratch is a file-scope
-// device array, one per device, whose address the host resolves once.
-// ---------------------------------------------------------------------------
+size_t ssa_attn_csr_size(const ssa_attn_params* p) {
+  if (!p || p->B < 1 || p->H < 1 || p->n_kv < 1 || p->N < 1 || p->M < 1 || p->Kn < 1 || p->H % p->n_kv)
+    return 0;
+  ssa::AttnDev a = attn_dev(p);
+  return ssa::attn_csr_layout(a, nullptr, nullptr);
+}
+
+int ssa_attn_build_csr(const ssa_attn_params* p, const void* nb, const uint8_t* valid, void* csr,
+                       size_t csr_bytes, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!p) return fail(SSA_ERR_INVALID, "params is NULL");
+  if (p->B < 1 || p->H < 1 || p->n_kv < 1 || p->N < 1 || p->M < 1 || p->Kn < 1)
+    return fail(SSA_ERR_INVALID, "B,H,n_kv,N,M,Kn must be >= 1");
+  if (p->H % p->n_kv)
+    return fail(SSA_ERR_INVALID, "num_heads (%d) must be divisible by num_kv_heads (%d)", p->H, p->n_kv);
+  if (!nb || !valid) return fail(SSA_ERR_INVALID, "neighbors/valid are NULL");
+  int rc;
+  if ((rc = check_edges(p))) return rc;
+  ssa::AttnDev a = attn_dev(p);
+  const size_t need_csr = ssa::attn_csr_layout(a, nullptr, nullptr);
+  if (!csr || csr_bytes < need_csr)
+    return fail(SSA_ERR_WORKSPACE, "csr buffer of %zu bytes needed, %zu given", need_csr, csr_bytes);
+  const size_t need = ssa::attn_bwd_workspace_layout(a, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need)
+    return fail(SSA_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  ssa::attn_bwd_workspace_layout(a, &a, workspace);
+  ssa::attn_csr_layout(a, &a, csr);
+  a.nb = nb; a.valid = valid;
+  cudaError_t e = ssa::launch_build_csr(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "inverted index launch");
+  return SSA_OK;
+}
+
+int ssa_attn_bwd_csr(const ssa_attn_params* p, const void* q, const void* k, const void* v,
+                     const void* nb, const uint8_t* valid, const void* dO, const float* lse, void* dq,
+                     void* dk, void* dv, const void* csr, size_t csr_bytes, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  int rc;
+  if ((rc = check_attn(p, q, k, v, nb, valid))) return rc;
+  if ((rc = check_rows("dO", dO, p->dtype, p->d, p->o_sb, p->o_sh, p->o_sn))) return rc;
+  if ((rc = check_rows("dq", dq, p->dtype, p->d, p->o_sb, p->o_sh, p->o_sn))) return rc;
+  if (!lse || !dk || !dv) return fail(SSA_ERR_INVALID, "lse/dk/dv are NULL");
+  if ((rc = check_edges(p))) return rc;
+  ssa::AttnDev a = attn_dev(p);
+  const size_t need_csr = ssa::attn_csr_layout(a, nullptr, nullptr);
+  if (!csr || csr_bytes < need_csr)
+    return fail(SSA_ERR_WORKSPACE, "csr buffer of %zu bytes needed, %zu given", need_csr, csr_bytes);
+  const size_t need = ssa::attn_bwd_workspace_layout(a, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need)
+    return fail(SSA_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  ssa::attn_bwd_workspace_layout(a, &a, workspace);
+  ssa::attn_csr_layout(a, &a, const_cast<void*>(csr));
+  a.q = q; a.k = k; a.v = v; a.nb = nb; a.valid = valid; a.dO = dO; a.lse_in = lse;
+  a.dq = dq; a.dk = dk; a.dv = dv;
+  cudaError_t e = ssa::launch_attn_bwd(a, false, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attention backward launch");
+  return SSA_OK;
+}
+
+// neighbor_overlap: per-row Jaccard similarity of two neighbor sets.
 int ssa_neighbor_overlap(const void* nb_a, const uint8_t* valid_a, const void* nb_b, const uint8_t* valid_b,
                          int64_t rows, int32_t K, int32_t nb_i64, float* out, void* stream) {
   if (rows < 0 || K < 1) return fail(SSA_ERR_INVALID, "rows=%lld, K=%d", (long long)rows, K);
@@ -316,8 +398,43 @@ int ssa_neighbor_overlap(const void* nb_a, const uint8_t* valid_a, const void* n
 
 int64_t ssa_kernel_launches(void) { return ssa::g_kernel_launches.load(std::memory_order_relaxed); }
 
+int ssa_graph_profile(int32_t enable) {
+  std::lock_guard<std::mutex> lock(ssa::g_prof_mu);
+  if (enable && !ssa::g_prof_on) {
+    for (int i = 0; i < ssa::kStageMarks; ++i) {
+      cudaError_t e = cudaEventCreate(&ssa::g_prof_ev[i]);
+      if (e != cudaSuccess) {
+        for (int j = 0; j < i; ++j) cudaEventDestroy(ssa::g_prof_ev[j]);
+        return cuda_fail(e, "cudaEventCreate (graph profiling)");
+      }
+    }
+    ssa::g_prof_on = true;
+  } else if (!enable && ssa::g_prof_on) {
+    ssa::g_prof_on = false;
+    for (int i = 0; i < ssa::kStageMarks; ++i) cudaEventDestroy(ssa::g_prof_ev[i]);
+  }
+  return SSA_OK;
+}
+
+int ssa_graph_stage_times(float* ms_out) {
+  std::lock_guard<std::mutex> lock(ssa::g_prof_mu);
+  if (!ms_out) return fail(SSA_ERR_INVALID, "ms_out is NULL");
+  if (!ssa::g_prof_on) return fail(SSA_ERR_INVALID, "graph profiling is off (ssa_graph_profile(1) first)");
+  cudaError_t e = cudaEventSynchronize(ssa::g_prof_ev[ssa::kStageMarks - 1]);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaEventSynchronize (graph profiling)");
+  for (int i = 0; i + 1 < ssa::kStageMarks; ++i) {
+    e = cudaEventElapsedTime(&ms_out[i], ssa::g_prof_ev[i], ssa::g_prof_ev[i + 1]);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventElapsedTime (graph profiling): no profiled build yet?");
+  }
+  return SSA_OK;
+}
+
 }  // extern "C"
 
+// ---------------------------------------------------------------------------
+// Attention backward without a caller workspace: the scratch is a file-scope
+// device array, one per device, whose address the host resolves once.
+// ---------------------------------------------------------------------------
 namespace {
 // Nothing in it has to start at zero: k_attn_bwd_rows writes every edge entry
 // (weight, dS, sort key, id) before the sort reads it, and the sort's
@@ -373,7 +490,7 @@ int ssa_attn_bwd_noalloc(const ssa_attn_params* p, const void* q, const void* k,
   ssa::attn_bwd_workspace_layout(a, &a, scratch);
   a.q = q; a.k = k; a.v = v; a.nb = nb; a.valid = valid; a.dO = dO; a.lse_in = lse;
   a.dq = dq; a.dk = dk; a.dv = dv;
-  cudaError_t e = ssa::launch_attn_bwd(a, static_cast<cudaStream_t>(stream));
+  cudaError_t e = ssa::launch_attn_bwd(a, true, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attention backward launch (static scratch)");
   return SSA_OK;
 }

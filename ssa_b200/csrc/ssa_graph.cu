@@ -42,50 +42,57 @@ namespace ssa {
 // ---------------------------------------------------------------------------
 // 1. Key hashing + bucket membership masks
 // ---------------------------------------------------------------------------
-template <int DT, int D>
-__global__ void __launch_bounds__(256) k_hash_keys(GraphDev g) {
-  extern __shared__ __align__(16) float s_planes[];  // R * p * d
+// Four lanes per key row (each holds a quarter of the row, see
+// proj_planes_x4), two rows per four lanes: a warp hashes its 32 keys
+// sixteen at a time, staging the codes in shared memory, then lane L takes
+// key L for the membership masks.
+template <int DT, int D, bool SMEM>
+__global__ void __launch_bounds__(256, 2) k_hash_keys(GraphDev g) {
+  extern __shared__ __align__(16) float s_planes[];  // SMEM: R * p * d floats; then the codes
   const int bg = blockIdx.y;
   const int b = bg / g.n_kv, gk = bg % g.n_kv;
   const int pd = g.p * g.d;
-  for (int i = threadIdx.x; i < g.R * pd; i += blockDim.x) {
-    const int r = i / pd, rem = i - r * pd;
-    s_planes[i] = g.rp[(int64_t)r * g.max_p * g.d + rem];
+  if (SMEM) {
+    for (int i = threadIdx.x * 4; i < g.R * pd; i += blockDim.x * 4) {
+      const int r = i / pd, rem = i - r * pd;
+      *reinterpret_cast<float4*>(s_planes + i) =
+          __ldg(reinterpret_cast<const float4*>(g.rp + (int64_t)r * g.max_p * g.d + rem));
+    }
   }
   __shared__ uint32_t s_pmax[8][64];  // per warp and round (R <= 64): packed max, reduced per block
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int sub = lane & 3;
+  // [warp][R][32] codes of the warp's keys
+  uint16_t* codes = reinterpret_cast<uint16_t*>(s_planes + (SMEM ? g.R * pd : 0)) + warp * g.R * 32;
   __syncthreads();
-  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  const int wbase = (blockIdx.x * 8 + warp) * 32;  // first key of the warp (a multiple of 32)
+  const void* kbase = row_ptr<DT>(g.k, b * g.k_sb + gk * g.k_sh);
+  constexpr int RW = 2, EPL = D / 4;  // two keys per four lanes
+  for (int i = 0; i < 2; ++i) {
+    float xs[RW * EPL];
+#pragma unroll
+    for (int w = 0; w < RW; ++w) {
+      const int mk = wbase + i * 16 + w * 8 + (lane >> 2);
+      load_slice_x4<DT, D>(row_ptr<DT>(kbase, (int64_t)(mk < g.M ? mk : 0) * g.k_sm), g.d, sub, mk < g.M,
+                           xs + w * EPL);
+    }
+    for (int r = 0; r < g.R; ++r) {
+      uint32_t code[RW] = {};
+      const float* pl = SMEM ? s_planes + r * pd : g.rp + (int64_t)r * g.max_p * g.d;
+      for_round_projections_x4<D, SMEM, RW>(xs, pl, g.d, g.p, sub, [&](int j, int w, float s) {
+        if (s > 0.f) code[w] |= 1u << j;  // proj > 0, strict (:589)
+      });
+      if (sub == 0)
+#pragma unroll
+        for (int w = 0; w < RW; ++w) codes[r * 32 + i * 16 + w * 8 + (lane >> 2)] = (uint16_t)code[w];
+    }
+  }
+  __syncwarp();
+  const int m = wbase + lane;
   const bool act = m < g.M;
   const unsigned amask = __ballot_sync(0xffffffffu, act);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int wbase = m - lane;  // multiple of 32
-  // The key row stays in registers for all R * p projections.
-  float x[D];
-  const void* row = row_ptr<DT>(g.k, b * g.k_sb + gk * g.k_sh + (int64_t)(act ? m : 0) * g.k_sm);
-#pragma unroll
-  for (int i = 0; i < D; i += 4) {
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (act && i < g.d) v = load4<DT>(row, i);
-    x[i] = v.x; x[i + 1] = v.y; x[i + 2] = v.z; x[i + 3] = v.w;
-  }
   for (int r = 0; r < g.R; ++r) {
-    uint32_t code = 0;
-    for (int j = 0; j < g.p; ++j) {
-      const float* pl = s_planes + (r * g.p + j) * g.d;
-      // even elements in the low half, odd ones in the high half, in order
-      unsigned long long s2 = 0ull;
-#pragma unroll
-      for (int t = 0; t < D; t += 4) {
-        if (t < g.d) {
-          const float4 w = *reinterpret_cast<const float4*>(pl + t);
-          s2 = f2_fma(f2_pack(x[t], x[t + 1]), f2_pack(w.x, w.y), s2);
-          s2 = f2_fma(f2_pack(x[t + 2], x[t + 3]), f2_pack(w.z, w.w), s2);
-        }
-      }
-      float s0, s1;
-      f2_unpack(s2, s0, s1);
-      if (s0 + s1 > 0.f) code |= 1u << j;  // proj > 0, strict (:589)
-    }
+    const uint32_t code = codes[r * 32 + lane];
     uint32_t mx = 0u;
     if (act) {
       g.kcode[((int64_t)bg * g.R + r) * g.M + m] = (uint16_t)code;
@@ -375,35 +382,41 @@ __global__ void k_merge_rows(MergeDev m) {
   }
 }
 
-// Query/key hash ids only (the reference's _hash), for the ssa_hash_ids API.
-template <int DT>
+// Query/key hash ids only (the reference's _hash), for the ssa_hash_ids API:
+// the same four-lanes-per-row projections as the graph build's kernels, so
+// the ids reported here are the ids the graph build uses.
+template <int DT, int D>
 __global__ void __launch_bounds__(256) k_hash_ids(const void* x, int B, int heads, int rows_n,
                                                   int d, int64_t sb, int64_t sh, int64_t sn,
                                                   const float* rp, int R, int max_p, int p,
                                                   int32_t* out) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  constexpr int RW = 2, EPL = D / 4;  // two rows per four lanes, sixteen per warp
+  const int lane = threadIdx.x & 31, sub = lane & 3;
+  const int64_t base = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * (8 * RW) + (lane >> 2);
   const int64_t total = (int64_t)B * heads * rows_n;
-  if (i >= total) return;
-  const int n = (int)(i % rows_n);
-  const int64_t bh = i / rows_n;
-  const int b = (int)(bh / heads), h = (int)(bh % heads);
-  const void* row = row_ptr<DT>(x, b * sb + h * sh + (int64_t)n * sn);
+  int64_t obase[RW];
+  int nn[RW];
+  bool act[RW];
+  float xs[RW * EPL];
+#pragma unroll
+  for (int w = 0; w < RW; ++w) {
+    const int64_t i = base + 8 * w;
+    act[w] = i < total;  // no early exit: the four lanes of a row shuffle together
+    const int64_t ii = act[w] ? i : 0;
+    nn[w] = (int)(ii % rows_n);
+    const int64_t bh = ii / rows_n;
+    const int b = (int)(bh / heads), h = (int)(bh % heads);
+    obase[w] = bh * R;
+    load_slice_x4<DT, D>(row_ptr<DT>(x, b * sb + h * sh + (int64_t)nn[w] * sn), d, sub, act[w], xs + w * EPL);
+  }
   for (int r = 0; r < R; ++r) {
-    uint32_t code = 0;
-    for (int j = 0; j < p; ++j) {
-      const float* pl = rp + ((int64_t)r * max_p + j) * d;
-      float s0 = 0.f, s1 = 0.f;
-      for (int t = 0; t < d; t += 4) {
-        const float4 v = load4<DT>(row, t);
-        const float4 w = __ldg(reinterpret_cast<const float4*>(pl + t));
-        s0 = fmaf(v.x, w.x, s0);
-        s1 = fmaf(v.y, w.y, s1);
-        s0 = fmaf(v.z, w.z, s0);
-        s1 = fmaf(v.w, w.w, s1);
-      }
-      if (s0 + s1 > 0.f) code |= 1u << j;
-    }
-    out[(bh * R + r) * rows_n + n] = (int32_t)code;
+    uint32_t code[RW] = {};
+    for_round_projections_x4<D, false, RW>(xs, rp + (int64_t)r * max_p * d, d, p, sub, [&](int j, int w, float s) {
+      if (s > 0.f) code[w] |= 1u << j;
+    });
+#pragma unroll
+    for (int w = 0; w < RW; ++w)
+      if (act[w] && sub == 0) out[(obase[w] + r) * rows_n + nn[w]] = (int32_t)code[w];
   }
 }
 
@@ -452,18 +465,24 @@ __global__ void __launch_bounds__(256) k_neighbor_overlap(const IT* nb_a, const 
 // ---------------------------------------------------------------------------
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+#ifndef SSA_SAMPLE_DIV
+#define SSA_SAMPLE_DIV 12
+#endif
+// The sample pass scores every (A / kSampleDiv)-th key tile.
+constexpr int kSampleDiv = SSA_SAMPLE_DIV;
+
 size_t graph_workspace_layout(GraphDev* g) {
   const int64_t BG = (int64_t)g->B * g->n_kv;
   const int64_t W = g->Wpad;
   const int64_t NB = int64_t(1) << g->p;
   const int64_t rows = (int64_t)g->B * g->H * g->N;
   g->capg = ((6 * g->A + 64) + 7) / 8 * 8;
-  // Every s-th key tile is sampled (about 12 / A of them); the sampled
-  // tiles' records must fit the row buffer.
+  // Every s-th key tile is sampled (about kSampleDiv / A of them); the
+  // sampled tiles' records must fit the row buffer.
   {
     const int tiles = (g->M + 127) / 128;
     const int fit = (int)((size_t)g->capg * 8 / kSampleTileBytes);
-    int s = g->A / 12 > 1 ? g->A / 12 : 1;
+    int s = g->A / kSampleDiv > 1 ? g->A / kSampleDiv : 1;
     if (fit > 0 && (tiles + s - 1) / s > fit) s = (tiles + fit - 1) / fit;
     g->sample_s = s;
   }
@@ -484,12 +503,13 @@ size_t graph_workspace_layout(GraphDev* g) {
   const size_t o_zero_end = off;
   const size_t o_bsize = take(sizeof(int32_t) * BG * g->R * NB);
   const size_t o_lastc = take(sizeof(int32_t) * BG * g->R * NB);
-  size_t o_qids = 0, o_qempty = 0, o_tau = 0, o_rcnt = 0, o_buf = 0;
+  size_t o_qids = 0, o_qempty = 0, o_tau = 0, o_rcnt = 0, o_buf = 0, o_sspec = 0;
   if (g->use_tc) {
     o_qids = take(sizeof(uint16_t) * rows * g->NT);
     o_qempty = take(rows);
     o_tau = take(sizeof(float) * rows);
     o_rcnt = take(sizeof(int32_t) * rows * 2);
+    o_sspec = take(sizeof(float) * rows * (g->R + 1));
     o_buf = take(sizeof(unsigned long long) * rows * g->capg);
   }
   if (g->ws) {
@@ -506,6 +526,7 @@ size_t graph_workspace_layout(GraphDev* g) {
       g->qempty = reinterpret_cast<uint8_t*>(base + o_qempty);
       g->tau = reinterpret_cast<float*>(base + o_tau);
       g->rcnt = reinterpret_cast<int32_t*>(base + o_rcnt);
+      g->sspec = reinterpret_cast<float*>(base + o_sspec);
       g->buf = reinterpret_cast<unsigned long long*>(base + o_buf);
     }
     g->zero_off = o_zero_begin;
@@ -565,36 +586,47 @@ static cudaError_t launch_select_dt(const GraphDev& g, int mode, int rows, size_
 
 cudaError_t launch_graph(const GraphDev& g, int mode, cudaStream_t st) {
   cudaError_t e;
+  stage_mark(kStageBegin, st);
   e = cudaMemsetAsync(static_cast<char*>(g.ws) + g.zero_off, 0, g.zero_bytes, st);
   if (e != cudaSuccess) return e;
   {
-    const size_t sm = (size_t)g.R * g.p * g.d * sizeof(float);
+    const size_t planes = (size_t)g.R * g.p * g.d * sizeof(float);
+    const bool smem = planes <= kHashPlaneSmemMax;
+    const size_t sm = (smem ? planes : 0) + (size_t)8 * g.R * 32 * sizeof(uint16_t);
     dim3 grid((g.M + 255) / 256, g.B * g.n_kv);
-    auto fn = g.dtype == kDtF32 ? (g.d <= 64 ? k_hash_keys<kDtF32, 64> : k_hash_keys<kDtF32, 128>)
-                                : (g.d <= 64 ? k_hash_keys<kDtBF16, 64> : k_hash_keys<kDtBF16, 128>);
+    const bool f32 = g.dtype == kDtF32;
+    auto fn = smem ? (g.d <= 64 ? (f32 ? k_hash_keys<kDtF32, 64, true> : k_hash_keys<kDtBF16, 64, true>)
+                                : (f32 ? k_hash_keys<kDtF32, 128, true> : k_hash_keys<kDtBF16, 128, true>))
+                   : (g.d <= 64 ? (f32 ? k_hash_keys<kDtF32, 64, false> : k_hash_keys<kDtBF16, 64, false>)
+                                : (f32 ? k_hash_keys<kDtF32, 128, false> : k_hash_keys<kDtBF16, 128, false>));
     if ((e = set_smem(fn, sm)) != cudaSuccess) return e;
     fn<<<grid, 256, sm, st>>>(g);
     note_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
+  stage_mark(kStageHashKeys, st);
   {
     const int64_t warps = (int64_t)g.B * g.n_kv * g.R * g.NB;
     k_bucket_trim<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(g);
   }
   note_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  stage_mark(kStageBucketTrim, st);
   GraphDev f = g;
   if (g.use_tc && select_tc_pointers_ok(g)) {
     if ((e = launch_select_tc(g, mode, st)) != cudaSuccess) return e;
     f.fallback_only = 1;  // exact FMA scan for the tiles the selection flagged
   } else {
+    for (int i = kStageHashQueries; i <= kStageRowsFinal; ++i) stage_mark(i, st);
     f.fallback_only = 0;
   }
   int rows;
   size_t smem;
   if (choose_select_rows(f, &rows, &smem)) return cudaErrorInvalidConfiguration;
-  return f.dtype == kDtF32 ? launch_select_dt<kDtF32>(f, mode, rows, smem, st)
-                           : launch_select_dt<kDtBF16>(f, mode, rows, smem, st);
+  e = f.dtype == kDtF32 ? launch_select_dt<kDtF32>(f, mode, rows, smem, st)
+                        : launch_select_dt<kDtBF16>(f, mode, rows, smem, st);
+  stage_mark(kStageSelectFma, st);
+  return e;
 }
 
 cudaError_t launch_merge(const MergeDev& m, cudaStream_t st) {
@@ -614,11 +646,11 @@ cudaError_t launch_hash_ids(const void* x, int dtype, int B, int heads, int rows
                             int64_t sb, int64_t sh, int64_t sn, const float* rp, int R,
                             int max_p, int p, int32_t* out, cudaStream_t st) {
   const int64_t total = (int64_t)B * heads * rows;
-  const unsigned grid = (unsigned)((total + 255) / 256);
-  if (dtype == kDtF32)
-    k_hash_ids<kDtF32><<<grid, 256, 0, st>>>(x, B, heads, rows, d, sb, sh, sn, rp, R, max_p, p, out);
-  else
-    k_hash_ids<kDtBF16><<<grid, 256, 0, st>>>(x, B, heads, rows, d, sb, sh, sn, rp, R, max_p, p, out);
+  const unsigned grid = (unsigned)((total + 127) / 128);  // 8 warps x 16 rows
+  const bool f32 = dtype == kDtF32;
+  auto fn = d <= 64 ? (f32 ? k_hash_ids<kDtF32, 64> : k_hash_ids<kDtBF16, 64>)
+                    : (f32 ? k_hash_ids<kDtF32, 128> : k_hash_ids<kDtBF16, 128>);
+  fn<<<grid, 256, 0, st>>>(x, B, heads, rows, d, sb, sh, sn, rp, R, max_p, p, out);
   note_launch();
   return cudaGetLastError();
 }

@@ -15,6 +15,7 @@ struct GraphDev {
   int R, max_p, p, C, Te, NT, NB, W, Wpad, A;
   int causal, is_cross, window, G, Wout;
   int row0;  // sequence position of query row 0 (query-row sharding)
+  uint32_t wait_limit;  // polls before a tensor-core scan wait gives up (ssa_debug_set_wait_limit)
   int64_t q_sb, q_sh, q_sn, k_sb, k_sh, k_sm;
   const void* q;
   const void* k;
@@ -35,6 +36,8 @@ struct GraphDev {
   uint8_t* qempty;                // [B*H*N] some slot's bucket is empty
   float* tau;                     // [B*H*N] scan threshold
   int32_t* rcnt;                  // [B*H*N][2] kept candidates per scan group (> capg/2: overflow)
+  float* sspec;                   // [B*H*N][R + 1] full-scan scores of the round-r pad key
+                                  // (r < R) and of causal self (R) -- keys the scan skips
   unsigned long long* buf;        // [B*H*N][capg] kept (key << 32 | score bits); in the
                                   // sample pass kSampleTileBytes records per sampled tile
   uint8_t* tile_flags;            // [B*H][ceil(N/128)] tiles for the exact fallback
@@ -48,6 +51,10 @@ struct GraphDev {
 // score halves (256 bytes) and the tile's 128-bit candidate mask.
 constexpr int kSampleTileBytes = 272;
 
+// The hashing kernels stage the R * p hyperplanes in shared memory when they
+// take at most this many bytes, and read them through L1 otherwise.
+constexpr size_t kHashPlaneSmemMax = 64 * 1024;
+
 // Index of the member mask of 64-key word w, round r, bucket u. The two words
 // of a 128-key tile are adjacent, so one tile's masks for all (round, bucket)
 // pairs form one contiguous block of R * NB * 16 bytes.
@@ -57,6 +64,23 @@ __host__ __device__ inline int64_t bmap_idx(const GraphDev& g, int bg, int w, in
 
 // Host-side count of kernel launches made by this library (ssa_kernel_launches).
 void note_launch();
+
+// Stage boundaries of a graph build (ssa_graph_profile / ssa_graph_stage_times):
+// stage i runs between marks i and i + 1.
+enum GraphStageMark {
+  kStageBegin = 0,
+  kStageHashKeys = 1,
+  kStageBucketTrim = 2,
+  kStageHashQueries = 3,
+  kStageScanSample = 4,
+  kStageRowsThresh = 5,
+  kStageScanFull = 6,
+  kStageRowsFinal = 7,
+  kStageSelectFma = 8,
+  kStageMarks = 9
+};
+// Records the profiling event of mark i on st while profiling is on.
+void stage_mark(int i, cudaStream_t st);
 
 // Fills the workspace pointers of g (g->ws may be null to only size it) and
 // returns the bytes needed. Decides g->use_tc from the shapes.
@@ -110,18 +134,28 @@ struct AttnDev {
   void* dv;
   float* ep;          // [rows][Kn] value weight per edge
   float* eds;         // [rows][Kn] scale * dS per edge
-  uint32_t* ekey;     // [rows][Kn] bg * M + key, or the sentinel BG * M
-  uint32_t* eid;      // [rows][Kn] edge id (row * Kn + slot)
-  uint32_t* skey;     // sorted keys
-  uint32_t* sid;      // edge ids in sorted order
-  uint32_t* seg;      // [B*n_kv*M + 1] first sorted position of each key
+  // inverted neighbor index (valid edges only, sorted by (kv slice, key))
+  uint32_t* skey;     // bg * M + key of each sorted edge
+  uint32_t* sid;      // edge id (row * Kn + slot) of each sorted edge
+  uint32_t* seg;      // [B*n_kv*M + 1] first sorted position of each key; [B*n_kv*M] = valid edges
+  // edge-sort temporaries
+  uint32_t* tk0;      // [rows * Kn] keys / ids between passes (ping-pong)
+  uint32_t* ti0;
+  uint32_t* tk1;
+  uint32_t* ti1;
+  uint32_t* cnt;      // [B*n_kv][256][tiles] digit counts, then offsets
+  uint32_t* tot;      // [B*n_kv] edges per slice in a pass
+  uint32_t* sbase;    // [B*n_kv + 1] output offset of each slice in the last pass
   float* part;        // [chunks][2][2][d] partial dk / dv of keys that cross a chunk edge
-  void* sort_tmp;
-  size_t sort_tmp_bytes;
 };
 
 cudaError_t launch_attn_fwd(const AttnDev& a, cudaStream_t st);
+// Workspace of the backward (per-edge arrays, sort temporaries, partials and
+// an inverted index of its own); bytes of a caller-held inverted index.
 size_t attn_bwd_workspace_layout(const AttnDev& a, AttnDev* out, void* ws);
-cudaError_t launch_attn_bwd(const AttnDev& a, cudaStream_t st);
+size_t attn_csr_layout(const AttnDev& a, AttnDev* out, void* csr);
+cudaError_t launch_build_csr(const AttnDev& a, cudaStream_t st);
+// build_csr: sort the edges first (else a.skey / sid / seg hold a built index).
+cudaError_t launch_attn_bwd(const AttnDev& a, bool build_csr, cudaStream_t st);
 
 }  // namespace ssa

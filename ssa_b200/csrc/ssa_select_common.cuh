@@ -154,36 +154,133 @@ __device__ __forceinline__ float dot_row_global(const float* q, const void* row,
   return (s0 + s1) + (s2 + s3);
 }
 
-// Projections of one row (x: D floats in registers, zero beyond d) onto NBK
-// hyperplanes pl, pl + d, ..., pl + (NBK-1) d. Each projection takes the same
-// operations in the same order as a lone dot product would -- even elements
-// accumulate into the low half of a paired fp32 FMA, odd ones into the high
-// half, in element order, and the projection is the sum of the halves -- so
-// the result is bit-identical however many hyperplanes share the pass; the
-// NBK chains only give the FMA pipe independent work.
+// Every hash projection (keys, queries, the FMA fallback scan, ssa_hash_ids)
+// is summed in one fixed order, so the kernels that split a row over four
+// lanes and the ones that keep it in one thread give bit-identical ids:
+//   * element t belongs to slice (t / 4) % 4 -- slices interleave in groups
+//     of four consecutive elements;
+//   * within a slice, groups are taken in ascending order; of each group the
+//     pairs (t, t+1) and (t+2, t+3) go through a paired fp32 FMA, so even
+//     elements accumulate into the low half and odd ones into the high half;
+//   * a slice's sum is low + high, and the projection is
+//     (slice0 + slice1) + (slice2 + slice3).
+// Elements at or past d are skipped.
+
+// Projections of one row (x: D floats in registers) onto NBK hyperplanes pl,
+// pl + d, ..., pl + (NBK-1) d, in the order above. The NBK chains only give
+// the FMA pipe independent work; each result is the same as a lone one.
 template <int NBK, int D, bool SMEM>
 __device__ __forceinline__ void proj_planes(const float* x, const float* pl, int d, float* out) {
-  unsigned long long s2[NBK];
+  unsigned long long s2[NBK][4];
 #pragma unroll
-  for (int k = 0; k < NBK; ++k) s2[k] = 0ull;
+  for (int k = 0; k < NBK; ++k)
+#pragma unroll
+    for (int s = 0; s < 4; ++s) s2[k][s] = 0ull;
 #pragma unroll
   for (int t = 0; t < D; t += 4) {
     if (t < d) {
+      const int s = (t >> 2) & 3;
       const unsigned long long xa = f2_pack(x[t], x[t + 1]), xb = f2_pack(x[t + 2], x[t + 3]);
 #pragma unroll
       for (int k = 0; k < NBK; ++k) {
         const float4 w = SMEM ? *reinterpret_cast<const float4*>(pl + k * d + t)
                               : __ldg(reinterpret_cast<const float4*>(pl + k * d + t));
-        s2[k] = f2_fma(xa, f2_pack(w.x, w.y), s2[k]);
-        s2[k] = f2_fma(xb, f2_pack(w.z, w.w), s2[k]);
+        s2[k][s] = f2_fma(xa, f2_pack(w.x, w.y), s2[k][s]);
+        s2[k][s] = f2_fma(xb, f2_pack(w.z, w.w), s2[k][s]);
       }
     }
   }
 #pragma unroll
   for (int k = 0; k < NBK; ++k) {
-    float s0, s1;
-    f2_unpack(s2[k], s0, s1);
-    out[k] = s0 + s1;
+    float v[4];
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      float lo, hi;
+      f2_unpack(s2[k][s], lo, hi);
+      v[s] = lo + hi;
+    }
+    out[k] = (v[0] + v[1]) + (v[2] + v[3]);
+  }
+}
+
+// The same projections with each row split over four consecutive lanes: lane
+// `sub` (0..3) holds slice `sub` of RW rows -- elements 16 i + 4 sub .. +3 --
+// as xs[r * EPL + 4 i .. + 3] (EPL = D / 4 floats per row). Each lane sums
+// its slices; two butterfly steps give every lane of the four (slice0 +
+// slice1) + (slice2 + slice3), bit-identical to proj_planes. Each hyperplane
+// element loaded serves RW rows. out[r * NBK + k]. All 32 lanes of the warp
+// must call it together.
+template <int NBK, int D, bool SMEM, int RW>
+__device__ __forceinline__ void proj_planes_x4(const float* xs, const float* pl, int d, int sub, float* out) {
+  constexpr int EPL = D / 4;
+  unsigned long long s2[RW * NBK];
+#pragma unroll
+  for (int k = 0; k < RW * NBK; ++k) s2[k] = 0ull;
+#pragma unroll
+  for (int i = 0; i < EPL; i += 4) {
+    const int t = 4 * i + 4 * sub;  // element index of xs[r * EPL + i]
+    if (t < d) {
+#pragma unroll
+      for (int k = 0; k < NBK; ++k) {
+        const float4 w = SMEM ? *reinterpret_cast<const float4*>(pl + k * d + t)
+                              : __ldg(reinterpret_cast<const float4*>(pl + k * d + t));
+        const unsigned long long wa = f2_pack(w.x, w.y), wb = f2_pack(w.z, w.w);
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+          s2[r * NBK + k] = f2_fma(f2_pack(xs[r * EPL + i], xs[r * EPL + i + 1]), wa, s2[r * NBK + k]);
+          s2[r * NBK + k] = f2_fma(f2_pack(xs[r * EPL + i + 2], xs[r * EPL + i + 3]), wb, s2[r * NBK + k]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < RW * NBK; ++k) {
+    float lo, hi;
+    f2_unpack(s2[k], lo, hi);
+    float v = lo + hi;
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    out[k] = v;
+  }
+}
+
+// Lane `sub`'s slice of a row (elements 16 i + 4 sub .. +3, zero at or past
+// d) into xs[EPL]. Rows are 8-byte (bf16) / 16-byte (fp32) aligned and d is
+// a multiple of 4, so every group of four is one aligned load.
+template <int DT, int D>
+__device__ __forceinline__ void load_slice_x4(const void* row, int d, int sub, bool act, float* xs) {
+#pragma unroll
+  for (int i = 0; i < D / 4; i += 4) {
+    const int t = 4 * i + 4 * sub;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (act && t < d) v = load4<DT>(row, t);
+    xs[i] = v.x; xs[i + 1] = v.y; xs[i + 2] = v.z; xs[i + 3] = v.w;
+  }
+}
+
+// f(j, r, proj) for hyperplanes j = 0 .. p-1 of one round and rows r < RW,
+// each row split over four lanes (see proj_planes_x4), two hyperplanes per
+// pass. j and r are compile-time indices in f, so f may write register
+// arrays at [j] / [r].
+template <int D, bool SMEM, int RW, typename F>
+__device__ __forceinline__ void for_round_projections_x4(const float* xs, const float* pl, int d, int p, int sub,
+                                                         F&& f) {
+#pragma unroll
+  for (int j = 0; j < 12; j += 2) {
+    if (j + 2 <= p) {
+      float o[2 * RW];
+      proj_planes_x4<2, D, SMEM, RW>(xs, pl + (size_t)j * d, d, sub, o);
+#pragma unroll
+      for (int r = 0; r < RW; ++r) {
+        f(j, r, o[r * 2]);
+        f(j + 1, r, o[r * 2 + 1]);
+      }
+    } else if (j < p) {
+      float o[RW];
+      proj_planes_x4<1, D, SMEM, RW>(xs, pl + (size_t)j * d, d, sub, o);
+#pragma unroll
+      for (int r = 0; r < RW; ++r) f(j, r, o[r]);
+    }
   }
 }
 

@@ -1,7 +1,8 @@
 // ssa_select_rows.cu -- per-query-row stages of the tensor-core graph build.
 //
-//   k_hash_queries  thread per query row: the row's bucket id per (round,
-//                   probe) slot and whether any of those buckets is empty.
+//   k_hash_queries  four lanes per query row: the row's bucket id per
+//                   (round, probe) slot and whether any of those buckets is
+//                   empty.
 //   k_rows          warp per query row, after a scan pass of k_scan_tc:
 //     THRESH mode   from the sampled candidates, tau = the x-th largest score
 //                   (x ~ 3A scaled by the sampled fraction of key tiles),
@@ -25,33 +26,90 @@ namespace ssa {
 // ---------------------------------------------------------------------------
 // Query hashing
 // ---------------------------------------------------------------------------
-template <int DT, int D>
-__global__ void __launch_bounds__(128) k_hash_queries(GraphDev g) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  uint16_t* tids = reinterpret_cast<uint16_t*>(smem);  // [NT][128]
-  const int t = threadIdx.x;
-  const int64_t row = (int64_t)blockIdx.x * 128 + t;
+// Four lanes per query row (each holds a quarter of the row, see
+// proj_planes_x4) and two rows per four lanes, sixteen rows per warp: each
+// hyperplane element read from shared memory serves two rows. Lane 0 of each
+// row's four writes its (round, probe) bucket offsets and the empty-bucket
+// flag.
+template <int DT, int D, bool SMEM>
+__global__ void __launch_bounds__(256, 2) k_hash_queries(GraphDev g) {
+  constexpr int RW = 2, EPL = D / 4;
+  extern __shared__ __align__(16) float s_planes[];  // SMEM: R * p hyperplanes of d floats
+  const int pd = g.p * g.d;
+  if (SMEM) {
+    for (int i = threadIdx.x * 4; i < g.R * pd; i += blockDim.x * 4) {
+      const int r = i / pd, rem = i - r * pd;
+      *reinterpret_cast<float4*>(s_planes + i) =
+          __ldg(reinterpret_cast<const float4*>(g.rp + (int64_t)r * g.max_p * g.d + rem));
+    }
+    __syncthreads();
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int sub = lane & 3;
   const int64_t total = (int64_t)g.B * g.H * g.N;
-  if (row >= total) return;
-  const int n = (int)(row % g.N);
-  const int64_t bh = row / g.N;
-  const int b = (int)(bh / g.H), h = (int)(bh % g.H);
-  const int bg = b * g.n_kv + h / g.rep;
-  float q[D];
-  const void* qrow = row_ptr<DT>(g.q, b * g.q_sb + h * g.q_sh + (int64_t)n * g.q_sn);
+  const int64_t base = ((int64_t)blockIdx.x * 8 + warp) * (8 * RW) + (lane >> 2);
+  int64_t rows[RW];
+  int bgs[RW];
+  bool writer[RW], empty[RW];
+  float xs[RW * EPL];
 #pragma unroll
-  for (int i = 0; i < D; i += 4) {
-    if (i < g.d) {
-      const float4 x = load4<DT>(qrow, i);
-      q[i] = x.x; q[i + 1] = x.y; q[i + 2] = x.z; q[i + 3] = x.w;
-    } else {
-      q[i] = q[i + 1] = q[i + 2] = q[i + 3] = 0.f;
+  for (int w = 0; w < RW; ++w) {
+    rows[w] = base + 8 * w;
+    const bool act = rows[w] < total;  // no early exit: the four lanes of a row shuffle together
+    const int64_t rr = act ? rows[w] : 0;
+    const int n = (int)(rr % g.N);
+    const int64_t bh = rr / g.N;
+    const int b = (int)(bh / g.H), h = (int)(bh % g.H);
+    bgs[w] = b * g.n_kv + h / g.rep;
+    writer[w] = act && sub == 0;
+    empty[w] = false;
+    load_slice_x4<DT, D>(row_ptr<DT>(g.q, b * g.q_sb + h * g.q_sh + (int64_t)n * g.q_sn), g.d, sub, act,
+                         xs + w * EPL);
+  }
+  for (int rd = 0; rd < g.R; ++rd) {
+    float proj[RW][12];
+    uint32_t id[RW];
+#pragma unroll
+    for (int w = 0; w < RW; ++w) {
+      id[w] = 0;
+#pragma unroll
+      for (int j = 0; j < 12; ++j) proj[w][j] = 0.f;
+    }
+    const float* pl = SMEM ? s_planes + rd * pd : g.rp + (int64_t)rd * g.max_p * g.d;
+    for_round_projections_x4<D, SMEM, RW>(xs, pl, g.d, g.p, sub, [&](int j, int w, float v) {
+      if (v > 0.f) id[w] |= 1u << j;  // proj > 0, strict (:589)
+      proj[w][j] = v;
+    });
+#pragma unroll
+    for (int w = 0; w < RW; ++w) {
+      if (!writer[w]) continue;
+      // primary bucket, then probe t flips the bit with the t-th smallest
+      // |proj| of the original id, ties in plane order (:599-646)
+      const int32_t* bs = g.bsize + (int64_t)(bgs[w] * g.R + rd) * g.NB;
+      const int tt0 = rd * (1 + g.Te);
+      g.qids[(int64_t)tt0 * total + rows[w]] = (uint16_t)(rd * g.NB + id[w]);
+      empty[w] |= __ldg(bs + id[w]) == 0;
+      uint32_t used = 0;
+      for (int t = 0; t < g.Te; ++t) {
+        int best = -1;
+        float bmag = 0.f;
+#pragma unroll
+        for (int j = 0; j < 12; ++j) {
+          if (j < g.p && !((used >> j) & 1u)) {
+            const float a = fabsf(proj[w][j]);
+            if (best < 0 || a < bmag) { best = j; bmag = a; }
+          }
+        }
+        used |= 1u << best;
+        const uint32_t pid = id[w] ^ (1u << best);
+        g.qids[(int64_t)(tt0 + 1 + t) * total + rows[w]] = (uint16_t)(rd * g.NB + pid);
+        empty[w] |= __ldg(bs + pid) == 0;
+      }
     }
   }
-  const bool empty = hash_row_ids<D>(g, q, bg, tids, 128, t);
-  for (int tt = 0; tt < g.NT; ++tt)
-    g.qids[(int64_t)tt * total + row] = (uint16_t)((tt / (1 + g.Te)) * g.NB + tids[tt * 128 + t]);
-  g.qempty[row] = empty ? 1 : 0;
+#pragma unroll
+  for (int w = 0; w < RW; ++w)
+    if (writer[w]) g.qempty[rows[w]] = empty[w] ? 1 : 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -452,7 +510,10 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
     const unsigned same = __match_any_sync(0xffffffffu, xs);  // every lane takes part
     const bool keep = xs >= 0 && lane == __ffs(same) - 1;
     const unsigned km = __ballot_sync(0xffffffffu, keep);
-    if (keep) S.spec[__popc(km & ((1u << lane) - 1u))] = xs;
+    // key in the low 24 bits; above them 1 + the slot of its full-scan score
+    // (pad key of round r: r; causal self: R), 0 if the scan keeps none
+    const int src1 = lane <= g.R ? lane + 1 : 0;
+    if (keep) S.spec[__popc(km & ((1u << lane) - 1u))] = xs | (src1 << 24);
     const int nspec = __popc(km);
     __syncwarp();
     const uint16_t* toffs = g.qids + row;  // slot tt at toffs[tt * total]: r * NB + bucket
@@ -463,7 +524,7 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
     // loads issued before any is used.
     auto replay = [&](int p) -> uint8_t {
       const int i = p / g.NT, tt = p - i * g.NT;
-      const int x = S.spec[i];
+      const int x = S.spec[i] & 0xFFFFFF;
       const int off = __ldg(toffs + (int64_t)tt * total);
       const int r = off >> g.p;
       const int u = off & (g.NB - 1);
@@ -510,11 +571,16 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
       }
     }
     __syncwarp();
-    // Lane i decides special i: eligible iff its first appearance is valid;
-    // an eligible key that the scan did not already keep needs its score.
-    bool need_dot = false;
+    // Lane i decides special i: eligible iff its first appearance is valid.
+    // An eligible key that the scan did not already keep needs its score:
+    // pad keys and causal self were scored by the full scan (sspec); any
+    // other (an empty-bucket fallback) gets a dot product below.
+    bool need_dot = false, captured = false;
+    int xk = 0;
     if (lane < nspec) {
-      const int x = S.spec[lane];
+      const int e = S.spec[lane];
+      xk = e & 0xFFFFFF;
+      const int src = (e >> 24) - 1;
       bool elig = false;
       for (int tt = 0; tt < g.NT; ++tt) {
         const uint8_t f = S.sflag[lane * g.NT + tt];
@@ -524,16 +590,32 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
       }
       if (elig) {
         const bool scanned =
-            !((__ldg(g.pmask + (int64_t)bg * g.Wpad + (x >> 6)) >> (x & 63)) & 1ull) && !(g.causal && x >= na);
-        bool present = false;
-        if (scanned)
-          for (int z = 0; z < c && !present; ++z) present = (int)S.ky[z] == x;
-        need_dot = !present;
+            !((__ldg(g.pmask + (int64_t)bg * g.Wpad + (xk >> 6)) >> (xk & 63)) & 1ull) && !(g.causal && xk >= na);
+        if (scanned) {
+          bool present = false;
+          for (int z = 0; z < c && !present; ++z) present = (int)S.ky[z] == xk;
+          need_dot = !present;
+        } else if (src >= 0) {
+          captured = true;
+        } else {
+          need_dot = true;
+        }
       }
     }
+    // Captured scores go right after the buffered entries.
+    const unsigned cpm = __ballot_sync(0xffffffffu, captured);
+    if (captured) {
+      const int src = (S.spec[lane] >> 24) - 1;
+      const int pos = c + __popc(cpm & ((1u << lane) - 1u));
+      const uint32_t u = okey(__ldg(g.sspec + row * (g.R + 1) + src));
+      S.ok[pos] = u;
+      S.ky[pos] = (uint16_t)xk;
+      note_key(u);
+    }
+    const int cc = c + __popc(cpm);
     const unsigned dm = __ballot_sync(0xffffffffu, need_dot);
     const int ndot = __popc(dm);
-    if (need_dot) S.spec[32 + __popc(dm & ((1u << lane) - 1u))] = S.spec[lane];
+    if (need_dot) S.spec[32 + __popc(dm & ((1u << lane) - 1u))] = xk;
     __syncwarp();
     // Scores of those keys: 8 lanes per key, D/8 elements per lane.
     if (ndot > 0) {
@@ -571,13 +653,13 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
         acc += __shfl_xor_sync(0xffffffffu, acc, 4);
         if (j < ndot && sub == 0) {
           const uint32_t u = okey(acc);
-          S.ok[c + j] = u;
-          S.ky[c + j] = (uint16_t)S.spec[32 + j];
+          S.ok[cc + j] = u;
+          S.ky[cc + j] = (uint16_t)S.spec[32 + j];
           note_key(u);
         }
       }
     }
-    const int tot = c + ndot;
+    const int tot = cc + ndot;
     __syncwarp();
 
     // Exact top-A (the whole pool when it has at most A entries). At least A
@@ -805,9 +887,23 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
     const int total = min(s0 + nlg + nwin, g.Wout);
     int32_t* nbo = g.nb + row * g.Wout;
     uint8_t* vo = g.valid + row * g.Wout;
-    for (int j = lane; j < g.Wout; j += 32) {
-      nbo[j] = j < total ? stage_out[j] : 0;
-      vo[j] = j < total ? 1 : 0;
+    if ((g.Wout & 3) == 0) {  // rows start 16-byte (nb) / 4-byte (valid) aligned: 4 slots per store
+      for (int j = lane * 4; j < g.Wout; j += 128) {
+        const int4 sv = *reinterpret_cast<const int4*>(stage_out + j);
+        int4 o;
+        o.x = j < total ? sv.x : 0;
+        o.y = j + 1 < total ? sv.y : 0;
+        o.z = j + 2 < total ? sv.z : 0;
+        o.w = j + 3 < total ? sv.w : 0;
+        *reinterpret_cast<int4*>(nbo + j) = o;
+        const int nv = min(max(total - j, 0), 4);  // leading valid slots of the four
+        *reinterpret_cast<uint32_t*>(vo + j) = nv >= 4 ? 0x01010101u : (0x01010101u & ((1u << (8 * nv)) - 1u));
+      }
+    } else {
+      for (int j = lane; j < g.Wout; j += 32) {
+        nbo[j] = j < total ? stage_out[j] : 0;
+        vo[j] = j < total ? 1 : 0;
+      }
     }
     for (int l = lane; l < nl1; l += 32) S.l1[l] = 0u;
     __syncwarp();
@@ -824,21 +920,26 @@ static cudaError_t smem_attr(F* fn, size_t bytes) {
 
 cudaError_t launch_hash_queries(const GraphDev& g, cudaStream_t st) {
   const int64_t rows = (int64_t)g.B * g.H * g.N;
-  const unsigned grid = (unsigned)((rows + 127) / 128);
-  const size_t sm = (size_t)g.NT * 128 * 2;
+  const unsigned grid = (unsigned)((rows + 127) / 128);  // 8 warps x 16 rows
+  const size_t planes = (size_t)g.R * g.p * g.d * sizeof(float);
+  const bool smem = planes <= kHashPlaneSmemMax;
+  const size_t sm = smem ? planes : 0;
   cudaError_t e;
+  auto run = [&](auto fn) {
+    if ((e = smem_attr(fn, sm)) != cudaSuccess) return;
+    fn<<<grid, 256, sm, st>>>(g);
+    note_launch();
+    e = cudaGetLastError();
+  };
+  const bool f32 = g.dtype == kDtF32;
   if (g.d <= 64) {
-    auto fn = g.dtype == kDtF32 ? k_hash_queries<kDtF32, 64> : k_hash_queries<kDtBF16, 64>;
-    if ((e = smem_attr(fn, sm)) != cudaSuccess) return e;
-    fn<<<grid, 128, sm, st>>>(g);
-    note_launch();
+    if (smem) run(f32 ? k_hash_queries<kDtF32, 64, true> : k_hash_queries<kDtBF16, 64, true>);
+    else run(f32 ? k_hash_queries<kDtF32, 64, false> : k_hash_queries<kDtBF16, 64, false>);
   } else {
-    auto fn = g.dtype == kDtF32 ? k_hash_queries<kDtF32, 128> : k_hash_queries<kDtBF16, 128>;
-    if ((e = smem_attr(fn, sm)) != cudaSuccess) return e;
-    fn<<<grid, 128, sm, st>>>(g);
-    note_launch();
+    if (smem) run(f32 ? k_hash_queries<kDtF32, 128, true> : k_hash_queries<kDtBF16, 128, true>);
+    else run(f32 ? k_hash_queries<kDtF32, 128, false> : k_hash_queries<kDtBF16, 128, false>);
   }
-  return cudaGetLastError();
+  return e;
 }
 
 size_t rows_smem_bytes(const GraphDev& g, int warps) { return (size_t)warps * rows_warp_bytes(g, 1); }

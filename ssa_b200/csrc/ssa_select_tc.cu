@@ -70,10 +70,11 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: about a few seconds at most, then flag the error.
+// Bounded wait: `limit` polls (2^24 by default: a few seconds at most),
+// then flag the error.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          int code) {
-  for (uint32_t i = 0; i < (1u << 24); ++i) {
+                                          int code, uint32_t limit) {
+  for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try(bar, parity)) return true;
     if (*abort) return false;
     if (i > 2048) __nanosleep(64);
@@ -86,8 +87,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // Warp-uniform version: every lane waits, and the warp proceeds only if all
 // lanes saw the phase complete (so .sync.aligned TMEM loads never diverge).
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                               int code) {
-  const bool ok = mbar_wait(bar, parity, abort, code);
+                                               int code, uint32_t limit) {
+  const bool ok = mbar_wait(bar, parity, abort, code, limit);
   return __all_sync(0xffffffffu, ok);
 }
 
@@ -170,6 +171,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// One fp32 column of this thread's TMEM lane.
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+  return __uint_as_float(r);
+}
+
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -190,7 +198,7 @@ __device__ __forceinline__ float pick32(const float* a, int j) {
 }
 
 struct SmemPlan {
-  uint32_t q, k, bm, toff, bars, tmem_slot, total;
+  uint32_t q, k, bm, toff, bars, tmem_slot, pads, total;
   int stages, bstages;
   uint32_t bm_bytes;
 };
@@ -217,6 +225,8 @@ __host__ __device__ inline SmemPlan plan_stages(int D, int NT, int stages, uint3
   p.toff = take((uint32_t)NT * ROWS * 2, 16);
   p.bars = take(24 * 8, 8);
   p.tmem_slot = take(16, 16);
+  p.pads = take(64 * 4 + 16 * 4, 16);  // pad keys perm_r[M-1] of the slice's rounds (R <= 64),
+                                       // then a bitmap of the key tiles holding one (M <= 65536)
   // At least 80 KB per CTA so that at most two CTAs share an SM: two CTAs
   // use all 512 TMEM columns, a third would wait in tcgen05.alloc.
   uint32_t total = off + 1024;
@@ -275,6 +285,7 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 13);
   uint64_t* bfull = bars + 14;      // [NB_ST] mask block loaded (bulk tx)
   uint64_t* bempty = bars + 18;     // [NB_ST] mask block read (the reading group's 4 warps)
+  uint64_t* mma_done = bars + 22;   // every MMA issued has completed (before TMEM is freed)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + sp.tmem_slot);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -303,6 +314,7 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
       mbar_init(bempty + i, 4);
     }
     mbar_init(qfull, 1);
+    mbar_init(mma_done, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -327,14 +339,14 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
       const unsigned long long* bmg = g.bmap + bmap_idx(g, bg, 0, 0, 0);
       for (int i = 0; i < ntl; ++i) {
         const int s = i % NS;
-        if (!mbar_wait(kempty + s, ((i / NS) & 1) ^ 1, abort_flag, 11)) break;
+        if (!mbar_wait(kempty + s, ((i / NS) & 1) ^ 1, abort_flag, 11, g.wait_limit)) break;
         mbar_expect_tx(kfull + s, ATOMS * NKEY * 128);
         for (int a = 0; a < ATOMS; ++a)
           tma_load_4d(ks + (s * ATOMS + a) * NKEY * 128, &kmap, kfull + s, a * 64, gk, i * step * NKEY, b);
         issued = i + 1;
         if (NB_ST) {
           const int sb2 = i % NB_ST;
-          if (!mbar_wait(bempty + sb2, ((i / NB_ST) & 1) ^ 1, abort_flag, 18)) break;
+          if (!mbar_wait(bempty + sb2, ((i / NB_ST) & 1) ^ 1, abort_flag, 18, g.wait_limit)) break;
           mbar_expect_tx(bfull + sb2, bmb);
           bulk_load(bms + sb2 * bmb, bmg + (int64_t)(i * step) * g.R * g.NB * 2, bmb, bfull + sb2);
           issued_b = i + 1;
@@ -347,12 +359,13 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && mbar_wait(qfull, 0, abort_flag, 13)) {
+    if (lane == 0 && mbar_wait(qfull, 0, abort_flag, 13, g.wait_limit)) {
       const uint32_t qa = smem_u32(qs);
+      int issued_mma = 0;
       for (int i = 0; i < ntl; ++i) {
         const int s = i % NS, sb = i & 1;
-        if (!mbar_wait(kfull + s, (i / NS) & 1, abort_flag, 14)) break;
-        if (!mbar_wait(sempty + sb, ((i >> 1) & 1) ^ 1, abort_flag, 15)) break;
+        if (!mbar_wait(kfull + s, (i / NS) & 1, abort_flag, 14, g.wait_limit)) break;
+        if (!mbar_wait(sempty + sb, ((i >> 1) & 1) ^ 1, abort_flag, 15, g.wait_limit)) break;
         tc_fence_after();
         const uint32_t ka = smem_u32(ks + s * ATOMS * NKEY * 128);
 #pragma unroll
@@ -363,6 +376,13 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
         }
         umma_commit(kempty + s);
         umma_commit(sfull + sb);
+        issued_mma = i + 1;
+      }
+      // The epilogue may have stopped early (a wait that ran out): wait for
+      // the MMAs in flight before TMEM is freed.
+      if (issued_mma) {
+        umma_commit(mma_done);
+        mbar_drain(mma_done, 0);
       }
     }
     __syncwarp();
@@ -376,10 +396,21 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
     const int n = n0 + t;
     const bool act = n < g.N;
     const int64_t row = (int64_t)bh * g.N + n;
+    int* pads = reinterpret_cast<int*>(smem + sp.pads);
     if (act && grp == 0)
       for (int tt = 0; tt < g.NT; ++tt)
         toff[tt * ROWS + t] = g.qids[(int64_t)tt * ((int64_t)g.B * g.H * g.N) + row];
-    asm volatile("bar.sync 1, 256;" ::: "memory");  // both groups see the offsets
+    uint32_t* padtiles = reinterpret_cast<uint32_t*>(pads + 64);
+    if (pass == 1 && warp == 0) {
+      if (lane < 16) padtiles[lane] = 0u;
+      __syncwarp();
+      for (int r = lane; r < g.R; r += 32) {
+        const int P = (int)(g.pmax[bg * g.R + r] & 0xFFFFFu);
+        pads[r] = P;
+        atomicOr(&padtiles[(P >> 7) >> 5], 1u << ((P >> 7) & 31));
+      }
+    }
+    asm volatile("bar.sync 1, 256;" ::: "memory");  // both groups see the offsets (and pad keys)
     const float thr = (pass == 1 && act) ? g.tau[row] : -INFINITY;
     const int half_cap = g.capg >> 1;
     unsigned long long* bo = g.buf + row * g.capg;      // sample records (pass 0)
@@ -395,7 +426,7 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
       unsigned long long w[2] = {0ull, 0ull};
       if (NB_ST) {
         const int sb2 = i % NB_ST;
-        if (!mbar_wait_warp(bfull + sb2, (i / NB_ST) & 1, abort_flag, 19)) break;
+        if (!mbar_wait_warp(bfull + sb2, (i / NB_ST) & 1, abort_flag, 19, g.wait_limit)) break;
         const uint4* bt = reinterpret_cast<const uint4*>(bms + sb2 * bmb);
         if (act)
           for (int tt = 0; tt < g.NT; ++tt) {
@@ -426,17 +457,25 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
           w[hw] = x;
         }
       }
-      if (!mbar_wait_warp(sfull + sb, (i >> 1) & 1, abort_flag, 16)) break;
+      const bool pad_tile = pass == 1 && ((padtiles[kt >> 5] >> (kt & 31)) & 1u);
+      // causal: the tile holds some row's own key (the last one or two tiles)
+      const bool self_tile = pass == 1 && g.causal && key0 <= g.row0 + n_hi && key0 + NKEY > g.row0 + n0;
+      if (!mbar_wait_warp(sfull + sb, (i >> 1) & 1, abort_flag, 16, g.wait_limit)) break;
       tc_fence_after();
       const uint32_t ta = tmem + ((uint32_t)((warp & 3) * 32) << 16) + sb * NKEY;
       unsigned char* tdst = reinterpret_cast<unsigned char*>(bo) + (size_t)i * kSampleTileBytes;
       const bool rec = pass == 0 && act && (size_t)(i + 1) * kSampleTileBytes <= (size_t)g.capg * 8;
+      // In the tiles holding a row's own key (causal) or a pad key, the
+      // scores of those keys -- which the scan leaves out but the selection
+      // may need -- are read from the accumulator after the candidates, so
+      // it is released only then.
+      const bool capture = pass == 1 && (self_tile || pad_tile);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {  // 32-column chunks
         float sc[32];
         tmem_ld32(ta + c * 32, sc);
         tmem_wait_ld();
-        if (c == 3) {  // the accumulator can be reused once all columns are read
+        if (c == 3 && !capture) {  // the accumulator can be reused once all columns are read
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(sempty + sb);
@@ -478,6 +517,34 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
             bh_out[cnt] = ((unsigned long long)(kbase32 + j) << 32) | __float_as_uint(pick32(sc, j));
           ++cnt;
         }
+      }
+      if (capture) {  // warp-uniform
+        if (pad_tile)
+          for (int r = 0; r < g.R; ++r) {
+            const int jp = pads[r] - key0;  // the same column for every row
+            if ((unsigned)jp < (unsigned)NKEY) {
+              const float v = tmem_ld1(ta + jp);
+              tmem_wait_ld();
+              if (act) g.sspec[row * (g.R + 1) + r] = v;
+            }
+          }
+        if (self_tile) {
+          // lane L's own key is column cb + L of the tile
+          const int cb = g.row0 + n0 + (warp & 3) * 32 - key0;
+          const int ch0 = cb >= 0 ? (cb >> 5) : -1;
+#pragma unroll 1
+          for (int ch = ch0; ch <= ch0 + 1; ++ch) {
+            if (ch < 0 || ch > 3) continue;
+            float sc[32];
+            tmem_ld32(ta + ch * 32, sc);
+            tmem_wait_ld();
+            const int js = cb + lane - ch * 32;
+            if (act && (unsigned)js < 32u) g.sspec[row * (g.R + 1) + g.R] = pick32(sc, js);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sempty + sb);
       }
       if (pass == 0) {
         if (rec)
@@ -573,10 +640,13 @@ cudaError_t launch_select_tc(const GraphDev& g, int mode, cudaStream_t st) {
   if (!make_map(&kmap, g.k, g.d, g.n_kv, g.M, g.B, g.k_sh, g.k_sm, g.k_sb)) return cudaErrorInvalidValue;
   cudaError_t e;
   if ((e = launch_hash_queries(g, st)) != cudaSuccess) return e;
+  stage_mark(kStageHashQueries, st);
   for (int pass = 0; pass < 2; ++pass) {
     e = g.d == 64 ? launch_scan_t<64>(g, pass, qmap, kmap, st) : launch_scan_t<128>(g, pass, qmap, kmap, st);
     if (e != cudaSuccess) return e;
+    stage_mark(pass == 0 ? kStageScanSample : kStageScanFull, st);
     if ((e = launch_rows(g, pass, mode, st)) != cudaSuccess) return e;
+    stage_mark(pass == 0 ? kStageRowsThresh : kStageRowsFinal, st);
   }
   return cudaSuccess;
 }

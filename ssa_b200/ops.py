@@ -263,9 +263,23 @@ def attn_fwd(q, k, v, nb, valid, scale: float, fp32w: bool, out: Optional[torch.
     return out, lse
 
 
-def attn_bwd(q, k, v, nb, valid, dO, lse, scale: float, fp32w: bool, dropout=None):
+class GraphCSR:
+    """Holder of one graph's inverted neighbor index (ssa_attn_build_csr): the
+    first backward that gets it builds the index, every later backward on
+    the same (neighbors, valid) reuses it -- the layers of a
+    CachedGraphSparseTransformer group share one."""
+
+    def __init__(self):
+        self.buf = None
+        self.key = None
+
+
+def attn_bwd(q, k, v, nb, valid, dO, lse, scale: float, fp32w: bool, dropout=None,
+             csr: Optional[GraphCSR] = None):
     """Gradients of sum(out * dO): dq (B,H,N,d), dk/dv (B,n_kv,M,d).
-    dropout: the (p, seed, offset) the forward used, or None."""
+    dropout: the (p, seed, offset) the forward used, or None. csr: a
+    GraphCSR shared by the backward passes over one graph, or None (the
+    index is then built inside this call)."""
     _require_cuda(q, k, v, nb, valid, dO, lse)
     q, *qs = _rows(q)
     k, *ks = _rows(k)
@@ -284,9 +298,22 @@ def attn_bwd(q, k, v, nb, valid, dO, lse, scale: float, fp32w: bool, dropout=Non
     L = _lib.load()
     ws_bytes = L.ssa_attn_bwd_workspace_size(ctypes.byref(p))
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
-    check(L.ssa_attn_bwd(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(nb), _ptr(valid), _ptr(dO),
-                         _ptr(lse.contiguous()), _ptr(dq), _ptr(dk), _ptr(dv), _ptr(ws), ws_bytes,
-                         _stream(q.device)), "ssa_attn_bwd")
+    st = _stream(q.device)
+    if csr is None:
+        check(L.ssa_attn_bwd(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(nb), _ptr(valid), _ptr(dO),
+                             _ptr(lse.contiguous()), _ptr(dq), _ptr(dk), _ptr(dv), _ptr(ws), ws_bytes, st),
+              "ssa_attn_bwd")
+        return dq, dk, dv
+    key = (tuple(nb.shape), nb.dtype, nb.data_ptr(), valid.data_ptr(), k.shape[1], k.shape[2])
+    if csr.buf is None or csr.key != key:
+        nbytes = L.ssa_attn_csr_size(ctypes.byref(p))
+        csr.buf = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
+        check(L.ssa_attn_build_csr(ctypes.byref(p), _ptr(nb), _ptr(valid), _ptr(csr.buf), nbytes, _ptr(ws),
+                                   ws_bytes, st), "ssa_attn_build_csr")
+        csr.key = key
+    check(L.ssa_attn_bwd_csr(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(nb), _ptr(valid), _ptr(dO),
+                             _ptr(lse.contiguous()), _ptr(dq), _ptr(dk), _ptr(dv), _ptr(csr.buf),
+                             csr.buf.numel(), _ptr(ws), ws_bytes, st), "ssa_attn_bwd_csr")
     return dq, dk, dv
 
 
@@ -295,24 +322,27 @@ class GatherAttention(torch.autograd.Function):
     the reference (routing decisions are sign tests and top-k)."""
 
     @staticmethod
-    def forward(ctx, q, k, v, nb, valid, scale, fp32w, dropout=None):
+    def forward(ctx, q, k, v, nb, valid, scale, fp32w, dropout=None, csr=None):
         out, lse = attn_fwd(q, k, v, nb, valid, scale, fp32w, dropout=dropout)
         ctx.save_for_backward(q, k, v, nb, valid, lse)
-        ctx.scale, ctx.fp32w, ctx.dropout = scale, fp32w, dropout
+        ctx.scale, ctx.fp32w, ctx.dropout, ctx.csr = scale, fp32w, dropout, csr
         ctx.mark_non_differentiable()
         return out
 
     @staticmethod
     def backward(ctx, dout):
         q, k, v, nb, valid, lse = ctx.saved_tensors
-        dq, dk, dv = attn_bwd(q, k, v, nb, valid, dout, lse, ctx.scale, ctx.fp32w, dropout=ctx.dropout)
-        return dq, dk, dv, None, None, None, None, None
+        dq, dk, dv = attn_bwd(q, k, v, nb, valid, dout, lse, ctx.scale, ctx.fp32w, dropout=ctx.dropout,
+                              csr=ctx.csr)
+        return dq, dk, dv, None, None, None, None, None, None
 
 
-def gather_attention(q, k, v, nb, valid, scale: float, fp32w: bool = False, dropout=None):
-    """dropout: None or (p, seed, offset); see new_dropout_key."""
+def gather_attention(q, k, v, nb, valid, scale: float, fp32w: bool = False, dropout=None,
+                     csr: Optional[GraphCSR] = None):
+    """dropout: None or (p, seed, offset); see new_dropout_key. csr: a
+    GraphCSR that the backward passes over this graph share."""
     if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
-        return GatherAttention.apply(q, k, v, nb, valid, scale, fp32w, dropout)
+        return GatherAttention.apply(q, k, v, nb, valid, scale, fp32w, dropout, csr)
     return attn_fwd(q, k, v, nb, valid, scale, fp32w, want_lse=False, dropout=dropout)[0]
 
 
@@ -335,3 +365,22 @@ def neighbor_overlap(nb_a: torch.Tensor, nb_b: torch.Tensor, valid_a: torch.Tens
     check(_lib.load().ssa_neighbor_overlap(_ptr(a), _ptr(va), _ptr(b), _ptr(vb), rows, K, int(i64),
                                            _ptr(out), _stream(nb_a.device)), "ssa_neighbor_overlap")
     return out
+
+
+class graph_profile:
+    """Context manager: graph builds inside it record per-stage CUDA events
+    (ssa_graph_profile); `times()` returns {stage: ms} of the most recent
+    build, waiting for it to finish."""
+
+    def __enter__(self):
+        check(_lib.load().ssa_graph_profile(1), "ssa_graph_profile")
+        return self
+
+    def times(self):
+        buf = (ctypes.c_float * len(_lib.GRAPH_STAGES))()
+        check(_lib.load().ssa_graph_stage_times(buf), "ssa_graph_stage_times")
+        return dict(zip(_lib.GRAPH_STAGES, [float(x) for x in buf]))
+
+    def __exit__(self, *exc):
+        _lib.load().ssa_graph_profile(0)
+        return False

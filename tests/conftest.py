@@ -20,6 +20,21 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200 / sm_100a)")
 
 
+def pytest_sessionfinish(session, exitstatus):
+    """Writes the parity counts the GPU tests recorded (tests/parity.py) to
+    the file named by SSA_PARITY_COUNTS, if set and anything was recorded."""
+    path = os.environ.get("SSA_PARITY_COUNTS")
+    if not path:
+        return
+    import json
+    import parity
+    if not parity.COUNTS:
+        return
+    with open(path, "w") as f:
+        json.dump({"band": {"hash_near_zero": 1e-6, "rescore_tie_rel": 64 * 2.0 ** -24},
+                   "cases": parity.COUNTS}, f, indent=1, sort_keys=True)
+
+
 @pytest.fixture(autouse=True)
 def _seed():
     torch.manual_seed(42)

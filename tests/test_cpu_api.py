@@ -115,7 +115,7 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(L, n), n
     assert set(names) == set(_lib.SIGNATURES), "ctypes signatures out of sync with the header"
-    assert L.ssa_abi_version() == 104
+    assert L.ssa_abi_version() == 105
 
 
 def test_static_scratch_size_matches_header():
@@ -146,6 +146,23 @@ def test_ctypes_layouts_match_header(tmp_path):
         assert offs[("g", f)] == getattr(_lib.GraphParams, f).offset, f
     for f in fields_a:
         assert offs[("a", f)] == getattr(_lib.AttnParams, f).offset, f
+
+
+def test_integration_stub_matches_header():
+    """The reference-side ctypes stub in INTEGRATION.md declares
+    ssa_graph_params field for field: same size and offsets as the header's
+    struct (which test_ctypes_layouts_match_header pins to _lib.GraphParams)."""
+    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    m = re.search(r"^class GraphParams\(ctypes\.Structure\):.*?(?=\n\n)", text, re.S | re.M)
+    assert m, "GraphParams stub not found in INTEGRATION.md"
+    ns = {"ctypes": ctypes}
+    exec(m.group(0), ns)
+    stub = ns["GraphParams"]
+    assert ctypes.sizeof(stub) == ctypes.sizeof(_lib.GraphParams)
+    assert [f for f, _ in stub._fields_] == [f for f, _ in _lib.GraphParams._fields_]
+    for f, _ in _lib.GraphParams._fields_:
+        assert getattr(stub, f).offset == getattr(_lib.GraphParams, f).offset, f
+        assert getattr(stub, f).size == getattr(_lib.GraphParams, f).size, f
 
 
 def _params(**kw):

@@ -16,7 +16,7 @@ import pytest
 import torch
 
 from oracle import oracle as O
-from parity import compare_graphs
+from parity import compare_graphs, hash_near_zero, record
 
 from ssa_b200 import ops
 from ssa_b200.workloads import WORKLOADS, make_module, make_x, project
@@ -81,6 +81,11 @@ def test_fullsize_graph_slice_matches_oracle(cfg, rows, cuda):
     res = compare_graphs(g_nb.cpu().numpy(), g_va.cpu().numpy().astype(bool), ora_nb, ora_valid,
                          qs_np, ks_np, 1)
     print(cfg, {kk: res[kk] for kk in ("rows", "mismatched", "ties")})
+    p_eff = lsh.compute_effective_p(w.M, lsh.C, lsh.max_P)
+    near = int(hash_near_zero(qs_np, rp, p_eff).sum() + hash_near_zero(ks_np, rp, p_eff).sum())
+    record(f"{cfg}_fullsize_slice", graph_rows=res["rows"], graph_mismatched=res["mismatched"],
+           graph_ties=res["ties"], graph_unexplained=res["unexplained"],
+           rows_near_zero_hash=near)
     assert res["unexplained"] == 0, res
     assert res["ties"] <= max(2, res["rows"] // 1000), res
 
