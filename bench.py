@@ -46,9 +46,12 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
-    ap.add_argument("--mode", default="fwd", choices=["fwd", "train"],
+    ap.add_argument("--mode", default="fwd", choices=["fwd", "train", "model"],
                     help="fwd: graph build + attention forward (the headline metric); train: "
-                         "graph build + attention forward + backward (one layer's attention core)")
+                         "graph build + attention forward + backward (one layer's attention core); "
+                         "model: the training-config model step (c4: 6-layer SparseTransformer with "
+                         "its vocab embedding, forward + out.sum().backward(), and the same with "
+                         "CachedGraphSparseTransformer(reuse_every=4) behind an embedding)")
     ap.add_argument("--impl", default="ssa", choices=["ssa", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -378,6 +381,91 @@ def run_long_context(args, dev, flush, world, rank):
             "config": workload_config(w)}
 
 
+def run_model(args):
+    """The training config's model step on one GPU: token ids -> embedding ->
+    6 sparse-transformer layers -> out.sum().backward() (the reference's own
+    training check, tests/test_gradients.py:17-18). SparseTransformer builds a
+    graph in every layer; CachedGraphSparseTransformer(reuse_every=4) builds
+    one per group of layers and reuses it (and its inverted index) in the
+    group's forward and backward."""
+    import torch
+    from ssa_b200 import _lib
+    from ssa_b200.attention import CachedGraphSparseTransformer, SparseTransformer
+    from ssa_b200.workloads import WORKLOADS
+    w = WORKLOADS[args.workload]
+    if args.batch:
+        w = type(w)(**{**w.__dict__, "B": args.batch})
+    if not w.layers or w.layers < 2:
+        raise SystemExit("--mode model is for the training config (c4)")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = w.config()
+    torch.manual_seed(0)
+    plain = SparseTransformer(cfg, num_layers=w.layers, vocab_size=w.vocab).to(dev)
+    torch.manual_seed(0)
+    embed = torch.nn.Embedding(w.vocab, w.d_model).to(dev)
+    cached = CachedGraphSparseTransformer(cfg, num_layers=w.layers, reuse_every=4).to(dev)
+    g = torch.Generator(device="cpu").manual_seed(1)
+    ids = torch.randint(0, w.vocab, (w.B, w.N), generator=g).to(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step_plain():
+        out, _ = plain(ids)
+        out.sum().backward()
+
+    def step_cached():
+        out, _ = cached(embed(ids))
+        out.sum().backward()
+
+    def fwd_only(fn):
+        with torch.no_grad():
+            fn()
+
+    def timed(fn, steps):
+        evs = []
+        for _ in range(steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        return statistics.mean(x.elapsed_time(y) for x, y in evs)
+
+    res = {}
+    clocks = ClockSampler(0)
+    launches, clk = 0, None
+    for name, fn, fwd in (("sparse_transformer", step_plain, lambda: plain(ids)),
+                          ("cached_graph_transformer", step_cached, lambda: cached(embed(ids)))):
+        for _ in range(max(args.warmup, 0)):
+            fn()
+        torch.cuda.synchronize()
+        if name == "sparse_transformer":
+            clocks.start()
+            launches0 = _lib.load().ssa_kernel_launches()
+        ms = timed(fn, args.steps)
+        if name == "sparse_transformer":
+            launches = _lib.load().ssa_kernel_launches() - launches0
+            clk = clocks.stop()
+        ms_fwd = timed(lambda: fwd_only(fwd), max(2, args.steps // 2))
+        res[name] = {"value": w.B * w.N / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+                     "forward_ms": ms_fwd, "backward_ms": ms - ms_fwd}
+        for p in list(plain.parameters()) + list(cached.parameters()) + list(embed.parameters()):
+            p.grad = None
+    main = res["sparse_transformer"]
+    out = {"metric": "sparse-transformer training step (forward + out.sum().backward()) tokens/s",
+           "value": main["value"], "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": main["ms_per_step"], "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None, "dtype": w.dtype,
+           "data": "synthetic (uniform random token ids; random-init weights in reference order)",
+           "config": {**workload_config(w), "layers": w.layers, "vocab": w.vocab},
+           "parallelism": "one GPU, whole job", "l2": "flushed (256 MB write) between timed steps",
+           "models": res, "gpu_launches": launches, "clocks": clk}
+    print(json.dumps(out))
+    return out
+
+
 def run_gpu(args):
     import torch
     import torch.distributed as dist
@@ -697,6 +785,8 @@ def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         run_reference(args)
+    elif args.mode == "model":
+        run_model(args)
     else:
         run_gpu(args)
 

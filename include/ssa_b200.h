@@ -211,9 +211,15 @@ SSA_API int ssa_attn_bwd_csr(const ssa_attn_params* p, const void* q, const void
  * device array of SSA_ATTN_BWD_STATIC_SCRATCH_BYTES (64 MiB) per device, so
  * the call allocates nothing; problems whose scratch
  * (ssa_attn_bwd_workspace_size) exceeds it are rejected with
- * SSA_ERR_WORKSPACE, about 2.5 million edges (B*H*N*Kn) at most.
+ * SSA_ERR_WORKSPACE. That is about 26 bytes per edge (B*H*N*Kn) at head dim
+ * 64, 28 at 128 and 32 at 256 while M < 65536 (8 more when M >= 65536: one
+ * more sort pass), so at most about 2.5, 2.3 and 2.0 million edges
+ * (1.9, 1.8 and 1.6 million for M >= 65536).
  *   - The first call on each device resolves the array's address with
- *     cudaGetSymbolAddress; make that first call before any stream capture.
+ *     cudaGetSymbolAddress and keeps it for the life of the process; make
+ *     that first call before any stream capture, and do not use this entry
+ *     point across a device reset (cudaDeviceReset or a new primary context
+ *     would leave the kept address stale).
  *   - Nothing in the scratch has to start at zero.
  *   - Calls share the device's one array: two calls whose executions overlap
  *     (other streams, or host threads without ordering between them) race on

@@ -86,3 +86,48 @@ def test_noalloc_rejects_oversized_problem(cuda):
     assert rc == _lib.SSA_ERR_WORKSPACE
     msg = L.ssa_last_error().decode()
     assert "static scratch" in msg and str(_lib.SSA_ATTN_BWD_STATIC_SCRATCH_BYTES) in msg
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_noalloc_limit_is_the_workspace_size(cuda, d):
+    """The largest problem whose scratch fits runs and matches the workspace
+    path; one query row more is rejected (the limit the header states is
+    ssa_attn_bwd_workspace_size <= SSA_ATTN_BWD_STATIC_SCRATCH_BYTES)."""
+    L = _lib.load()
+    B, H, n_kv, M, Kn = 1, 8, 2, 8192, 128
+    probe = torch.empty(1, H, 1, d, device=cuda, dtype=torch.bfloat16)
+    kv = torch.empty(B, n_kv, M, d, device=cuda, dtype=torch.bfloat16)
+
+    def need(N):
+        p = _params(probe.expand(B, H, N, d), kv, kv,
+                    torch.empty(B, H, N, Kn, device=cuda, dtype=torch.int32),
+                    torch.empty(B, H, N, d, device=cuda, dtype=torch.bfloat16), 1.0)
+        return L.ssa_attn_bwd_workspace_size(ctypes.byref(p))
+    lo, hi = 1, 1 << 16
+    while lo < hi:
+        mid = (lo + hi + 1) // 2
+        lo, hi = (mid, hi) if need(mid) <= _lib.SSA_ATTN_BWD_STATIC_SCRATCH_BYTES else (lo, mid - 1)
+    N = lo
+    assert 2.0e6 <= B * H * N * Kn <= 2.6e6  # the header's "about 2.5 / 2.3 million edges"
+    q, k, v, nb, valid, dO = _problem(cuda, torch.bfloat16, B=B, H=H, n_kv=n_kv, N=N, M=M, d=d, Kn=Kn)
+    scale = d ** -0.5
+    _, lse = ops.attn_fwd(q, k, v, nb, valid, scale, False, want_lse=True)
+    ref = ops.attn_bwd(q, k, v, nb, valid, dO, lse, scale, False)
+    p = _params(q, k, v, nb, dO, scale)
+    valid_u8 = valid.contiguous().view(torch.uint8)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
+    outs = [torch.full_like(dO, float("nan")), torch.full_like(k, float("nan")), torch.full_like(v, float("nan"))]
+    rc = L.ssa_attn_bwd_noalloc(ctypes.byref(p), ops._ptr(q), ops._ptr(k), ops._ptr(v), ops._ptr(nb),
+                                ops._ptr(valid_u8), ops._ptr(dO), ops._ptr(lse), *[ops._ptr(t) for t in outs],
+                                stream)
+    assert rc == _lib.SSA_OK, L.ssa_last_error().decode()
+    torch.cuda.synchronize(cuda)
+    for got, r in zip(outs, ref):
+        assert _rel(got, r) <= TOL[torch.bfloat16]
+    p.N = N + 1
+    assert need(N + 1) > _lib.SSA_ATTN_BWD_STATIC_SCRATCH_BYTES
+    rc = L.ssa_attn_bwd_noalloc(ctypes.byref(p), ops._ptr(q), ops._ptr(k), ops._ptr(v), ops._ptr(nb),
+                                ops._ptr(valid_u8), ops._ptr(dO), ops._ptr(lse), *[ops._ptr(t) for t in outs],
+                                stream)
+    assert rc == _lib.SSA_ERR_WORKSPACE
+    assert L.ssa_device_error(1) == 0
