@@ -467,22 +467,35 @@ __global__ void __launch_bounds__(128, 8) k_rows(GraphDev g) {
       }
     };
     // Two entries per 16-byte load (each half starts 16-byte aligned; an odd
-    // count's last load also reads the unused slot after it, inside the half).
+    // count's last load also reads the unused slot after it, inside the half),
+    // four loads in flight per lane.
     for (int hf = 0; hf < 2; ++hf) {
       const int ch = hf ? cnt1 : cnt0;
       const ulonglong2* src = reinterpret_cast<const ulonglong2*>(bo + (hf ? half_cap : 0));
       const int base = hf ? cnt0 : 0;
-      for (int pi = lane; 2 * pi < ch; pi += 32) {
-        const ulonglong2 e2 = __ldcs(src + pi);  // read once
-        const uint32_t u0 = okey(__uint_as_float((uint32_t)e2.x));
-        S.ok[base + 2 * pi] = u0;
-        S.ky[base + 2 * pi] = (uint16_t)(e2.x >> 32);
-        note_key(u0);
-        if (2 * pi + 1 < ch) {
-          const uint32_t u1 = okey(__uint_as_float((uint32_t)e2.y));
-          S.ok[base + 2 * pi + 1] = u1;
-          S.ky[base + 2 * pi + 1] = (uint16_t)(e2.y >> 32);
-          note_key(u1);
+      constexpr int U = 4;  // loads in flight per lane before any is used
+      for (int p0 = lane; 2 * p0 < ch; p0 += 32 * U) {
+        ulonglong2 e[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int pi = p0 + 32 * u;
+          e[u] = 2 * pi < ch ? __ldcs(src + pi) : make_ulonglong2(0ull, 0ull);  // read once
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int pi = p0 + 32 * u;
+          if (2 * pi < ch) {
+            const uint32_t u0 = okey(__uint_as_float((uint32_t)e[u].x));
+            S.ok[base + 2 * pi] = u0;
+            S.ky[base + 2 * pi] = (uint16_t)(e[u].x >> 32);
+            note_key(u0);
+            if (2 * pi + 1 < ch) {
+              const uint32_t u1 = okey(__uint_as_float((uint32_t)e[u].y));
+              S.ok[base + 2 * pi + 1] = u1;
+              S.ky[base + 2 * pi + 1] = (uint16_t)(e[u].y >> 32);
+              note_key(u1);
+            }
+          }
         }
       }
     }
