@@ -228,6 +228,31 @@ __device__ __forceinline__ unsigned long long raw_pair(const RawSlice<DT, EPL>& 
   }
 }
 
+// 32-bit word cp (elements 2 cp, 2 cp + 1) of a raw bf16 slice.
+template <int DT, int EPL>
+__device__ __forceinline__ uint32_t raw_word(const RawSlice<DT, EPL>& r, int cp) {
+  const uint4 w = r.w[cp >> 2];
+  return (cp & 3) == 0 ? w.x : (cp & 3) == 1 ? w.y : (cp & 3) == 2 ? w.z : w.w;
+}
+
+#ifndef SSA_ATTN_MIXED_FMA
+#define SSA_ATTN_MIXED_FMA 1
+#endif
+
+// lo += a.lo * b.lo, hi += a.hi * b.hi for packed bf16 pairs, with the
+// sm_100 mixed-precision FMA (bf16 operands, fp32 accumulate): the products
+// of bf16 values are exact in fp32, so this is bit for bit the fp32 FMA of
+// the widened values -- without the widening instructions.
+__device__ __forceinline__ void bf2_fma(uint32_t a, uint32_t b, float& lo, float& hi) {
+  asm("{\n\t.reg .b16 al, ah, bl, bh;\n\t"
+      "mov.b32 {al, ah}, %2;\n\t"
+      "mov.b32 {bl, bh}, %3;\n\t"
+      "fma.rn.f32.bf16 %0, al, bl, %0;\n\t"
+      "fma.rn.f32.bf16 %1, ah, bh, %1;\n\t}"
+      : "+f"(lo), "+f"(hi)
+      : "r"(a), "r"(b));
+}
+
 // Occupancy over rows in flight: for bf16 d = 128, 2 rows per 8-lane group at
 // 4 blocks (32 warps) per SM measured 5.90 ms at c2, against 6.25 ms for 4
 // rows at 3 blocks (the gathers hit L2; more warps hide their latency better).
@@ -270,11 +295,16 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? (DT == kDtF32 ? 2 : 4) : 4))
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      unsigned long long x2 = 0ull;
+      float xl = 0.f, xh = 0.f;
+      if constexpr (DT == kDtBF16 && SSA_ATTN_MIXED_FMA) {
 #pragma unroll
-      for (int c = 0; c < EPL / 2; ++c) x2 = f2_fma(q2[c], raw_pair<DT, EPL>(kr[u], c), x2);
-      float xl, xh;
-      f2_unpack(x2, xl, xh);
+        for (int c = 0; c < EPL / 2; ++c) bf2_fma(raw_word<DT, EPL>(qr, c), raw_word<DT, EPL>(kr[u], c), xl, xh);
+      } else {
+        unsigned long long x2 = 0ull;
+#pragma unroll
+        for (int c = 0; c < EPL / 2; ++c) x2 = f2_fma(q2[c], raw_pair<DT, EPL>(kr[u], c), x2);
+        f2_unpack(x2, xl, xh);
+      }
       float x = xl + xh;
       x += __shfl_xor_sync(0xffffffffu, x, 1);
       x += __shfl_xor_sync(0xffffffffu, x, 2);
@@ -304,10 +334,15 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? (DT == kDtF32 ? 2 : 4) : 4))
     s[j] = p;
   }
   __syncwarp();
-  // Pass 2: weighted sum of value rows.
+  // Pass 2: weighted sum of value rows. With bf16 weights (the reference's
+  // cast to v.dtype) the weight is a bf16 value too, so the mixed FMA applies.
+  constexpr bool kMixedPV = DT == kDtBF16 && !FP32W && SSA_ATTN_MIXED_FMA;
   unsigned long long acc2[EPL / 2];
+  float acc[EPL];
 #pragma unroll
   for (int c = 0; c < EPL / 2; ++c) acc2[c] = 0ull;
+#pragma unroll
+  for (int c = 0; c < EPL; ++c) acc[c] = 0.f;
   for (int j0 = 0; j0 < a.Kn; j0 += 4 * U) {
     RawSlice<DT, EPL> vrw[U];
     float p[U];
@@ -321,14 +356,22 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? (DT == kDtF32 ? 2 : 4) : 4))
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const unsigned long long pp = f2_pack(p[u], p[u]);
+      if constexpr (kMixedPV) {
+        const uint32_t pb = __float_as_uint(p[u]);
+        const uint32_t pw = (pb >> 16) | (pb & 0xffff0000u);  // the weight in both bf16 halves
 #pragma unroll
-      for (int c = 0; c < EPL / 2; ++c) acc2[c] = f2_fma(pp, raw_pair<DT, EPL>(vrw[u], c), acc2[c]);
+        for (int c = 0; c < EPL / 2; ++c) bf2_fma(pw, raw_word<DT, EPL>(vrw[u], c), acc[2 * c], acc[2 * c + 1]);
+      } else {
+        const unsigned long long pp = f2_pack(p[u], p[u]);
+#pragma unroll
+        for (int c = 0; c < EPL / 2; ++c) acc2[c] = f2_fma(pp, raw_pair<DT, EPL>(vrw[u], c), acc2[c]);
+      }
     }
   }
-  float acc[EPL];
+  if constexpr (!kMixedPV) {
 #pragma unroll
-  for (int c = 0; c < EPL / 2; ++c) f2_unpack(acc2[c], acc[2 * c], acc[2 * c + 1]);
+    for (int c = 0; c < EPL / 2; ++c) f2_unpack(acc2[c], acc[2 * c], acc[2 * c + 1]);
+  }
 #pragma unroll
   for (int c = 0; c < EPL; ++c) {
     acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], 8);

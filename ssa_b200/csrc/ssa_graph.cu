@@ -43,9 +43,9 @@ namespace ssa {
 // 1. Key hashing + bucket membership masks
 // ---------------------------------------------------------------------------
 // Four lanes per key row (each holds a quarter of the row, see
-// proj_planes_x4), two rows per four lanes: a warp hashes its 32 keys
-// sixteen at a time, staging the codes in shared memory, then lane L takes
-// key L for the membership masks.
+// proj_planes_x4), kHashRows<D> rows per four lanes: a warp hashes its 32
+// keys 8 * kHashRows<D> at a time, staging the codes in shared memory, then
+// lane L takes key L for the membership masks.
 template <int DT, int D, bool SMEM>
 __global__ void __launch_bounds__(256, 2) k_hash_keys(GraphDev g) {
   extern __shared__ __align__(16) float s_planes[];  // SMEM: R * p * d floats; then the codes
@@ -67,12 +67,12 @@ __global__ void __launch_bounds__(256, 2) k_hash_keys(GraphDev g) {
   __syncthreads();
   const int wbase = (blockIdx.x * 8 + warp) * 32;  // first key of the warp (a multiple of 32)
   const void* kbase = row_ptr<DT>(g.k, b * g.k_sb + gk * g.k_sh);
-  constexpr int RW = 2, EPL = D / 4;  // two keys per four lanes
-  for (int i = 0; i < 2; ++i) {
+  constexpr int RW = kHashRows<D>, EPL = D / 4;  // keys per four lanes
+  for (int i = 0; i < 32 / (8 * RW); ++i) {
     float xs[RW * EPL];
 #pragma unroll
     for (int w = 0; w < RW; ++w) {
-      const int mk = wbase + i * 16 + w * 8 + (lane >> 2);
+      const int mk = wbase + i * 8 * RW + w * 8 + (lane >> 2);
       load_slice_x4<DT, D>(row_ptr<DT>(kbase, (int64_t)(mk < g.M ? mk : 0) * g.k_sm), g.d, sub, mk < g.M,
                            xs + w * EPL);
     }
@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(256, 2) k_hash_keys(GraphDev g) {
       });
       if (sub == 0)
 #pragma unroll
-        for (int w = 0; w < RW; ++w) codes[r * 32 + i * 16 + w * 8 + (lane >> 2)] = (uint16_t)code[w];
+        for (int w = 0; w < RW; ++w) codes[r * 32 + i * 8 * RW + w * 8 + (lane >> 2)] = (uint16_t)code[w];
     }
   }
   __syncwarp();
@@ -390,7 +390,7 @@ __global__ void __launch_bounds__(256) k_hash_ids(const void* x, int B, int head
                                                   int d, int64_t sb, int64_t sh, int64_t sn,
                                                   const float* rp, int R, int max_p, int p,
                                                   int32_t* out) {
-  constexpr int RW = 2, EPL = D / 4;  // two rows per four lanes, sixteen per warp
+  constexpr int RW = kHashRows<D>, EPL = D / 4;  // rows per four lanes
   const int lane = threadIdx.x & 31, sub = lane & 3;
   const int64_t base = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * (8 * RW) + (lane >> 2);
   const int64_t total = (int64_t)B * heads * rows_n;
@@ -646,7 +646,8 @@ cudaError_t launch_hash_ids(const void* x, int dtype, int B, int heads, int rows
                             int64_t sb, int64_t sh, int64_t sn, const float* rp, int R,
                             int max_p, int p, int32_t* out, cudaStream_t st) {
   const int64_t total = (int64_t)B * heads * rows;
-  const unsigned grid = (unsigned)((total + 127) / 128);  // 8 warps x 16 rows
+  const int per_block = 64 * (d <= 64 ? kHashRows<64> : kHashRows<128>);  // 8 warps x 8 * RW rows
+  const unsigned grid = (unsigned)((total + per_block - 1) / per_block);
   const bool f32 = dtype == kDtF32;
   auto fn = d <= 64 ? (f32 ? k_hash_ids<kDtF32, 64> : k_hash_ids<kDtBF16, 64>)
                     : (f32 ? k_hash_ids<kDtF32, 128> : k_hash_ids<kDtBF16, 128>);

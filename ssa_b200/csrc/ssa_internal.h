@@ -54,6 +54,11 @@ constexpr int kSampleTileBytes = 272;
 // The hashing kernels stage the R * p hyperplanes in shared memory when they
 // take at most this many bytes, and read them through L1 otherwise.
 constexpr size_t kHashPlaneSmemMax = 64 * 1024;
+// Rows each group of four lanes hashes at once (a row is split over the
+// four): every hyperplane element loaded serves that many rows. The
+// registers of D / 4 floats per row set the count.
+template <int D>
+constexpr int kHashRows = D <= 64 ? 4 : 2;
 
 // Index of the member mask of 64-key word w, round r, bucket u. The two words
 // of a 128-key tile are adjacent, so one tile's masks for all (round, bucket)

@@ -33,7 +33,7 @@ namespace ssa {
 // flag.
 template <int DT, int D, bool SMEM>
 __global__ void __launch_bounds__(256, 2) k_hash_queries(GraphDev g) {
-  constexpr int RW = 2, EPL = D / 4;
+  constexpr int RW = 2, EPL = D / 4;  // the probes' projections take registers too: two rows
   extern __shared__ __align__(16) float s_planes[];  // SMEM: R * p hyperplanes of d floats
   const int pd = g.p * g.d;
   if (SMEM) {
