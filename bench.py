@@ -63,6 +63,8 @@ def parse_args(argv=None):
                     help="(batch, kv-group) slices in the CPU baseline sample")
     ap.add_argument("--no-long-context", action="store_true",
                     help="skip the second measurement of the long-context config c3 on the same GPUs")
+    ap.add_argument("--no-other-workloads", action="store_true",
+                    help="skip the c1 / c5 / c4 objects of the default run")
     ap.add_argument("--no-graph-profile", action="store_true",
                     help="skip the per-stage timing of the graph build after the timed steps")
     return ap.parse_args(argv)
@@ -381,24 +383,45 @@ def run_long_context(args, dev, flush, world, rank):
             "config": workload_config(w)}
 
 
-def run_model(args):
-    """The training config's model step on one GPU: token ids -> embedding ->
-    6 sparse-transformer layers -> out.sum().backward() (the reference's own
-    training check, tests/test_gradients.py:17-18). SparseTransformer builds a
-    graph in every layer; CachedGraphSparseTransformer(reuse_every=4) builds
-    one per group of layers and reuses it (and its inverted index) in the
-    group's forward and backward."""
+def run_other_workloads(args, dev, flush, world, rank):
+    """The other named configs on the same GPUs, fewer steps each: c1 and c5
+    (graph build + gather attention; group sharding when world > 1) and, on
+    one GPU, the c4 training step. One object per config, so one bench.py
+    run records a throughput for every named shape."""
+    import torch
+    from ssa_b200.workloads import WORKLOADS, make_module
+    steps, warmup = max(2, min(args.steps, 5)), max(3, min(args.warmup, 3))
+    stream = torch.cuda.current_stream(dev)
+    out = {}
+    for name in ("c1", "c5"):
+        w = WORKLOADS[name]
+        plan = "single" if world == 1 else ("groups" if w.B * w.n_kv >= world else "rows")
+        m = make_module(w, dev)
+        job = _Job(plan, w, m, dev, world, rank)
+        ms, ms_graph = time_job(job, stream, flush, steps, warmup, world, dev)
+        out[name] = {"value": w.B * w.N / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+                     "graph_build_ms": ms_graph, "steps": steps, "warmup": warmup, "dtype": w.dtype,
+                     "parallelism": "one GPU, whole job" if plan == "single" else
+                     f"group sharding: {w.B * w.n_kv} (batch, kv-head) units over {world} GPUs",
+                     "config": workload_config(w)}
+        del job, m
+    if world == 1:
+        w = WORKLOADS["c4"]
+        res, _, _ = model_step_times(w, dev, steps, warmup, flush)
+        out["c4"] = {"metric": "sparse-transformer training step (forward + out.sum().backward()) tokens/s",
+                     "steps": steps, "warmup": warmup, "dtype": w.dtype,
+                     "config": {**workload_config(w), "layers": w.layers, "vocab": w.vocab},
+                     "models": res}
+    return out
+
+
+def model_step_times(w, dev, steps, warmup, flush, clocks=None):
+    """Times the c4 model step of SparseTransformer and of
+    CachedGraphSparseTransformer(reuse_every=4) on one GPU; returns
+    ({model: times}, kernel launches of the first, its clock record)."""
     import torch
     from ssa_b200 import _lib
     from ssa_b200.attention import CachedGraphSparseTransformer, SparseTransformer
-    from ssa_b200.workloads import WORKLOADS
-    w = WORKLOADS[args.workload]
-    if args.batch:
-        w = type(w)(**{**w.__dict__, "B": args.batch})
-    if not w.layers or w.layers < 2:
-        raise SystemExit("--mode model is for the training config (c4)")
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
     cfg = w.config()
     torch.manual_seed(0)
     plain = SparseTransformer(cfg, num_layers=w.layers, vocab_size=w.vocab).to(dev)
@@ -407,7 +430,6 @@ def run_model(args):
     cached = CachedGraphSparseTransformer(cfg, num_layers=w.layers, reuse_every=4).to(dev)
     g = torch.Generator(device="cpu").manual_seed(1)
     ids = torch.randint(0, w.vocab, (w.B, w.N), generator=g).to(dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
     def step_plain():
         out, _ = plain(ids)
@@ -434,25 +456,47 @@ def run_model(args):
         return statistics.mean(x.elapsed_time(y) for x, y in evs)
 
     res = {}
-    clocks = ClockSampler(0)
     launches, clk = 0, None
     for name, fn, fwd in (("sparse_transformer", step_plain, lambda: plain(ids)),
                           ("cached_graph_transformer", step_cached, lambda: cached(embed(ids)))):
-        for _ in range(max(args.warmup, 0)):
+        for _ in range(max(warmup, 0)):
             fn()
         torch.cuda.synchronize()
         if name == "sparse_transformer":
-            clocks.start()
+            if clocks is not None:
+                clocks.start()
             launches0 = _lib.load().ssa_kernel_launches()
-        ms = timed(fn, args.steps)
+        ms = timed(fn, steps)
         if name == "sparse_transformer":
             launches = _lib.load().ssa_kernel_launches() - launches0
-            clk = clocks.stop()
-        ms_fwd = timed(lambda: fwd_only(fwd), max(2, args.steps // 2))
+            if clocks is not None:
+                clk = clocks.stop()
+        ms_fwd = timed(lambda: fwd_only(fwd), max(2, steps // 2))
         res[name] = {"value": w.B * w.N / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
                      "forward_ms": ms_fwd, "backward_ms": ms - ms_fwd}
         for p in list(plain.parameters()) + list(cached.parameters()) + list(embed.parameters()):
             p.grad = None
+    return res, launches, clk
+
+
+def run_model(args):
+    """The training config's model step on one GPU: token ids -> embedding ->
+    6 sparse-transformer layers -> out.sum().backward() (the reference's own
+    training check, tests/test_gradients.py:17-18). SparseTransformer builds a
+    graph in every layer; CachedGraphSparseTransformer(reuse_every=4) builds
+    one per group of layers and reuses it (and its inverted index) in the
+    group's forward and backward."""
+    import torch
+    from ssa_b200.workloads import WORKLOADS
+    w = WORKLOADS[args.workload]
+    if args.batch:
+        w = type(w)(**{**w.__dict__, "B": args.batch})
+    if not w.layers or w.layers < 2:
+        raise SystemExit("--mode model is for the training config (c4)")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    res, launches, clk = model_step_times(w, dev, args.steps, args.warmup, flush, ClockSampler(0))
     main = res["sparse_transformer"]
     out = {"metric": "sparse-transformer training step (forward + out.sum().backward()) tokens/s",
            "value": main["value"], "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
@@ -572,10 +616,13 @@ def run_gpu(args):
     if not args.no_e2e and args.mode == "fwd":
         e2e = run_e2e(args, job, dev, flush, world)
 
-    # The long-context config on the same GPUs, as a second object.
-    long_ctx = None
+    # The long-context config on the same GPUs, as a second object; then the
+    # other named configs.
+    long_ctx, others = None, None
     if args.workload == "c2" and args.mode == "fwd" and not args.batch and not args.no_long_context:
         long_ctx = run_long_context(args, dev, flush, world, rank)
+    if args.workload == "c2" and args.mode == "fwd" and not args.batch and not args.no_other_workloads:
+        others = run_other_workloads(args, dev, flush, world, rank)
 
     result = None
     if rank == 0:
@@ -623,6 +670,7 @@ def run_gpu(args):
             "e2e": e2e,
             "cpu_baseline": cpu,
             "long_context": long_ctx,
+            "other_workloads": others,
         }
         print(json.dumps(result))
     if world > 1:

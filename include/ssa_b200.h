@@ -79,6 +79,31 @@ typedef struct {
  * G + A (merge_neighbors, sparse_attention.py:1071-1076). */
 SSA_API int32_t ssa_graph_width(const ssa_graph_params* p);
 
+/*
+ * Fused QKV projection + LSH hash (the projections feeding the graph build,
+ * sparse_attention.py:1484-1486, and _hash of their q / k, :588-597):
+ *   qkv_out (B*N, (H + 2 n_kv) d) bf16 = x (B*N, d_model) bf16 times w_qkv^T,
+ *   w_qkv = [Wq; Wk; Wv] ((H + 2 n_kv) d, d_model) bf16 (nn.Linear weights
+ *   stacked), fp32 accumulation; and, from the bf16 q / k values, the graph
+ *   build's hash state (key bucket ids and member masks, query bucket ids)
+ *   written into `workspace`. Then ssa_build_graph_prehashed with the same
+ *   params and workspace finishes the graph; the result equals
+ *   ssa_build_graph on q / k views of qkv_out.
+ * p describes the self-attention graph (M == N, bf16) with q / k strides of
+ * those views: q_sb = k_sb = N (H + 2 n_kv) d, q_sh = k_sh = d,
+ * q_sn = k_sm = (H + 2 n_kv) d (k starts at column H d of qkv_out).
+ * ssa_qkv_proj_hash_supported returns 1 when this path serves p and d_model
+ * (head dim 64 / 128, N % 128 == 0, d_model % 64 == 0, (H + 2 n_kv) d % 128
+ * == 0, the tensor-core graph path), else 0.
+ */
+SSA_API int32_t ssa_qkv_proj_hash_supported(const ssa_graph_params* p, int32_t d_model);
+SSA_API int ssa_qkv_proj_hash(const ssa_graph_params* p, int32_t d_model, const void* x, const void* w_qkv,
+                              void* qkv_out, const float* rand_proj, void* workspace, size_t workspace_bytes,
+                              void* stream);
+SSA_API int ssa_build_graph_prehashed(const ssa_graph_params* p, const void* q, const void* k,
+                                      const float* rand_proj, const int32_t* glob, int32_t* nb_out,
+                                      uint8_t* valid_out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Bytes of device workspace ssa_build_graph / ssa_lsh_select need. */
 SSA_API size_t ssa_graph_workspace_size(const ssa_graph_params* p);
 
@@ -255,6 +280,25 @@ SSA_API int32_t ssa_device_error(int32_t clear);
  * and returns; ssa_device_error reports the code and that build's output is
  * undefined. Process-wide; read when each build is launched. */
 SSA_API int ssa_debug_set_wait_limit(uint32_t polls);
+
+/* Testing aids for the tensor-core hash (no counterpart in the reference;
+ * the hash ids are the same either way). Process-wide; read when each build
+ * is launched.
+ *   ssa_debug_set_hash: use_tc = 0 hashes keys and queries with the fp32 FMA
+ *     kernels only; else bf16 inputs with head dim 64 or 128 hash on the
+ *     tensor cores (the default). eps_c is the constant c of the bound
+ *     eps = c * |x|_2 * max_j |P[r][j]|_2 under which a projection is
+ *     recomputed in fp32 (0: the default 2^-14; larger values recompute
+ *     more, up to every projection).
+ *   ssa_debug_hash_dump: while buf (device, n_floats fp32) is set and holds
+ *     B*H*N*R*p_eff floats, each build writes the tensor-core projection of
+ *     query row i, round r, plane j to buf[(i * R + r) * p_eff + j]
+ *     (rows not hashed on the tensor cores are left as they are). NULL: off.
+ *   ssa_debug_hash_recomputed: (row, round) items recomputed in fp32 since
+ *     the last clear (synchronises with the device); -1 on error. */
+SSA_API int ssa_debug_set_hash(int32_t use_tc, float eps_c);
+SSA_API int ssa_debug_hash_dump(float* buf, int64_t n_floats);
+SSA_API int64_t ssa_debug_hash_recomputed(int32_t clear);
 
 /* Human-readable text for the last error on this host thread. */
 SSA_API const char* ssa_last_error(void);

@@ -70,6 +70,14 @@ SIGNATURES = {
     "ssa_neighbor_overlap": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp]),
     "ssa_device_error": (_i32, [_i32]),
     "ssa_debug_set_wait_limit": (ctypes.c_int, [ctypes.c_uint32]),
+    "ssa_qkv_proj_hash_supported": (_i32, [ctypes.POINTER(GraphParams), _i32]),
+    "ssa_qkv_proj_hash": (ctypes.c_int, [ctypes.POINTER(GraphParams), _i32, _vp, _vp, _vp, _vp, _vp, _sz,
+                                         _vp]),
+    "ssa_build_graph_prehashed": (ctypes.c_int, [ctypes.POINTER(GraphParams), _vp, _vp, _vp, _vp, _vp, _vp,
+                                                 _vp, _sz, _vp]),
+    "ssa_debug_set_hash": (ctypes.c_int, [_i32, ctypes.c_float]),
+    "ssa_debug_hash_dump": (ctypes.c_int, [ctypes.c_void_p, _i64]),
+    "ssa_debug_hash_recomputed": (_i64, [_i32]),
     "ssa_last_error": (ctypes.c_char_p, []),
     "ssa_abi_version": (_i32, []),
     "ssa_kernel_launches": (_i64, []),

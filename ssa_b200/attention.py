@@ -248,6 +248,40 @@ def sparse_gather_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 # ---------------------------------------------------------------------------
 # SparseAttention (sparse_attention.py:1206-1510)
 # ---------------------------------------------------------------------------
+class _FusedQKVHash(torch.autograd.Function):
+    """x -> qkv = x [Wq; Wk; Wv]^T (B, N, (H + 2 n_kv) d) through the fused
+    projection + hash kernel; its graph state goes to state[0] (None, and a
+    plain matmul, when the kernel does not serve the shapes). Backward: the
+    projection's gradients (dx = dqkv W, dW = dqkv^T x)."""
+
+    @staticmethod
+    def forward(ctx, x, wq, wk, wv, attn, causal, state):
+        w = torch.cat([wq, wk, wv], dim=0)
+        lsh = attn.lsh_builder
+        N = x.shape[1]
+        res = ops.qkv_project_hash(x, w, lsh.rand_proj, attn._glob(N, x.device), H=attn.H, n_kv=attn.n_kv,
+                                   R=lsh.R, max_p=lsh.max_P, p_eff=lsh.compute_effective_p(N, lsh.C, lsh.max_P),
+                                   C=lsh.C, T=lsh.T, A=lsh.output_width(N, attn.lsh_k), causal=causal,
+                                   K=attn.K, window=attn.config.window_size)
+        if res is None:
+            qkv = torch.nn.functional.linear(x, w)
+            state.append(None)
+        else:
+            qkv = res[0]
+            state.append(res[1])
+        ctx.save_for_backward(x, w)
+        ctx.splits = (wq.shape[0], wk.shape[0], wv.shape[0])
+        return qkv
+
+    @staticmethod
+    def backward(ctx, gq):
+        x, w = ctx.saved_tensors
+        dx = gq @ w
+        dw = gq.reshape(-1, gq.shape[-1]).t() @ x.reshape(-1, x.shape[-1])
+        dwq, dwk, dwv = torch.split(dw, ctx.splits, dim=0)
+        return dx, dwq, dwk, dwv, None, None, None
+
+
 class SparseAttention(nn.Module):
     """Sparse multi-head attention over a window + global + LSH neighbor
     graph. Self-attention (key_value None) or cross-attention (no window,
@@ -290,6 +324,11 @@ class SparseAttention(nn.Module):
                                            num_probes=config.lsh_num_probes)
         self.dp = config.dropout
         self._glob_cache = {}
+        # bf16 self-attention: True routes Wq / Wk / Wv through the fused QKV
+        # projection + hash kernel (ssa_qkv_proj_hash) where it serves the
+        # shapes. Off by default: cuBLAS's GEMM plus the tensor-core hash is
+        # faster today.
+        self.fuse_qkv = False
 
     # -- layout helpers (sparse_attention.py:1300-1323) ----------------------
     def _split_q(self, x):
@@ -362,10 +401,21 @@ class SparseAttention(nn.Module):
         src = key_value if is_cross else x
         M = src.shape[1]
         causal = self.config.causal and not is_cross
-        q = self._split_q(self.Wq(x))
-        k = self._split_kv_grouped(self.Wk(src))
-        v = self._split_kv_grouped(self.Wv(src))
-        nb, valid = self._graph(q, k, M, causal, is_cross)
+        fused = None
+        if not is_cross and x.dtype == torch.bfloat16 and self.fuse_qkv:
+            # One tcgen05 GEMM for Wq / Wk / Wv whose epilogue also hashes q
+            # and k for the graph (None when the shapes are not served).
+            state = []
+            qkv = _FusedQKVHash.apply(x, self.Wq.weight, self.Wk.weight, self.Wv.weight, self, causal, state)
+            if state[0] is not None:
+                q, k, v = ops.split_qkv(qkv, self.H, self.n_kv)
+                nb, valid = ops.build_graph_prehashed(q, k, state[0])
+                fused = True
+        if fused is None:
+            q = self._split_q(self.Wq(x))
+            k = self._split_kv_grouped(self.Wk(src))
+            v = self._split_kv_grouped(self.Wv(src))
+            nb, valid = self._graph(q, k, M, causal, is_cross)
         drop = ops.new_dropout_key(self.dp) if (self.dp > 0.0 and self.training) else None
         out = ops.gather_attention(q, k, v, nb, valid, self.scale, self.config.fp32_attn_weights,
                                    dropout=drop)

@@ -20,8 +20,8 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 OBJ_DIR = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libssa_b200.so")
-SOURCES = ["ssa_graph.cu", "ssa_select_tc.cu", "ssa_select_rows.cu", "ssa_attn.cu", "ssa_capi.cu"]
-HEADERS = ["ssa_common.cuh", "ssa_internal.h", "ssa_select_common.cuh"]
+SOURCES = ["ssa_graph.cu", "ssa_select_tc.cu", "ssa_hash_tc.cu", "ssa_select_rows.cu", "ssa_attn.cu", "ssa_capi.cu"]
+HEADERS = ["ssa_common.cuh", "ssa_internal.h", "ssa_select_common.cuh", "ssa_tcgen05.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr"]

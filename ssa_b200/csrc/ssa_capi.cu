@@ -82,6 +82,13 @@ int check_graph(const ssa_graph_params* p) {
 // Polls before a tensor-core scan wait gives up (ssa_debug_set_wait_limit);
 // 0: the default, 2^24.
 std::atomic<uint32_t> g_wait_limit{0};
+// Hashing on the tensor cores where supported (ssa_debug_set_hash), the
+// certification constant c (0: the default 2^-14), and the projection dump.
+std::atomic<int> g_hash_tc{1};
+std::atomic<float> g_hash_eps{0.f};
+std::mutex g_dump_mu;
+float* g_dump = nullptr;
+int64_t g_dump_n = 0;
 
 ssa::GraphDev dev_of(const ssa_graph_params* p) {
   ssa::GraphDev g;
@@ -100,6 +107,13 @@ ssa::GraphDev dev_of(const ssa_graph_params* p) {
   g.Wout = graph_width(p);
   g.q_sb = p->q_sb; g.q_sh = p->q_sh; g.q_sn = p->q_sn;
   g.k_sb = p->k_sb; g.k_sh = p->k_sh; g.k_sm = p->k_sm;
+  g.use_tc_hash = g_hash_tc.load(std::memory_order_relaxed);
+  const float c = g_hash_eps.load(std::memory_order_relaxed);
+  g.hash_eps = c > 0.f ? c : 1.f / 16384.f;
+  {
+    std::lock_guard<std::mutex> lk(g_dump_mu);
+    if (g_dump && g_dump_n >= (int64_t)p->B * p->H * p->N * p->R * p->p_eff) g.hash_dump = g_dump;
+  }
   return g;
 }
 
@@ -145,13 +159,33 @@ extern "C" {
 
 const char* ssa_last_error(void) { return g_err; }
 
-int32_t ssa_abi_version(void) { return 105; }
+int32_t ssa_abi_version(void) { return 106; }
 
 int32_t ssa_device_error(int32_t clear) { return ssa::read_device_error(clear); }
 
 int ssa_debug_set_wait_limit(uint32_t polls) {
   g_wait_limit.store(polls, std::memory_order_relaxed);
   return SSA_OK;
+}
+
+int ssa_debug_set_hash(int32_t use_tc, float eps_c) {
+  if (!(eps_c >= 0.f) || eps_c > 1.f) return fail(SSA_ERR_INVALID, "eps_c must be in [0, 1]");
+  g_hash_tc.store(use_tc ? 1 : 0, std::memory_order_relaxed);
+  g_hash_eps.store(eps_c, std::memory_order_relaxed);
+  return SSA_OK;
+}
+
+int ssa_debug_hash_dump(float* buf, int64_t n_floats) {
+  if (buf && n_floats < 0) return fail(SSA_ERR_INVALID, "n_floats must be >= 0");
+  std::lock_guard<std::mutex> lk(g_dump_mu);
+  g_dump = buf;
+  g_dump_n = buf ? n_floats : 0;
+  return SSA_OK;
+}
+
+int64_t ssa_debug_hash_recomputed(int32_t clear) {
+  const unsigned long long v = ssa::read_hash_recomputed(clear);
+  return v == ~0ull ? -1 : (int64_t)v;
 }
 
 int32_t ssa_graph_width(const ssa_graph_params* p) { return p ? graph_width(p) : -1; }
@@ -164,7 +198,7 @@ size_t ssa_graph_workspace_size(const ssa_graph_params* p) {
 
 static int run_graph(const ssa_graph_params* p, const void* q, const void* k, const float* rp,
                      const int32_t* glob, int32_t* nb_out, uint8_t* valid_out, int32_t* lsh_out,
-                     void* ws, size_t ws_bytes, void* stream, int mode) {
+                     void* ws, size_t ws_bytes, void* stream, int mode, int prehashed = 0) {
   int rc;
   if ((rc = check_graph(p))) return rc;
   if ((rc = check_graph_inputs(p, q, k, rp, glob))) return rc;
@@ -179,6 +213,11 @@ static int run_graph(const ssa_graph_params* p, const void* q, const void* k, co
   g.q = q; g.k = k; g.rp = rp; g.glob = glob;
   g.lsh = lsh_out; g.nb = nb_out; g.valid = valid_out;
   if ((rc = check_select_fits(g))) return rc;  // the FMA scan is also the exact fallback
+  if (prehashed) {
+    if (!g.use_tc || !g.use_tc_hash || !ssa::select_tc_pointers_ok(g))
+      return fail(SSA_ERR_UNSUPPORTED, "a prehashed build needs the tensor-core path (ssa_qkv_proj_hash_supported)");
+    g.prehashed = 1;
+  }
   cudaError_t e = ssa::launch_graph(g, mode, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "graph build launch");
   return SSA_OK;
@@ -189,6 +228,60 @@ int ssa_build_graph(const ssa_graph_params* p, const void* q, const void* k, con
                     void* workspace, size_t workspace_bytes, void* stream) {
   return run_graph(p, q, k, rand_proj, glob, nb_out, valid_out, lsh_out, workspace,
                    workspace_bytes, stream, 0);
+}
+
+// The q / k views of a fused projection output: (B, N, H + 2 n_kv, d) rows.
+static bool proj_strides_ok(const ssa_graph_params* p) {
+  const int64_t n_out = (int64_t)(p->H + 2 * p->n_kv) * p->d;
+  return p->q_sb == (int64_t)p->N * n_out && p->q_sh == p->d && p->q_sn == n_out &&
+         p->k_sb == (int64_t)p->N * n_out && p->k_sh == p->d && p->k_sm == n_out;
+}
+
+int32_t ssa_qkv_proj_hash_supported(const ssa_graph_params* p, int32_t d_model) {
+  if (!p || check_graph(p)) return 0;
+  ssa::GraphDev g = dev_of(p);
+  ssa::graph_workspace_layout(&g);
+  return (g.use_tc && g.use_tc_hash && ssa::proj_hash_supported(g, d_model) && proj_strides_ok(p)) ? 1 : 0;
+}
+
+int ssa_qkv_proj_hash(const ssa_graph_params* p, int32_t d_model, const void* x, const void* w_qkv,
+                      void* qkv_out, const float* rand_proj, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  int rc;
+  if ((rc = check_graph(p))) return rc;
+  if (!ssa_qkv_proj_hash_supported(p, d_model))
+    return fail(SSA_ERR_UNSUPPORTED,
+                "fused projection + hash needs bf16 self-attention, head dim 64/128, N %% 128 == 0, "
+                "d_model %% 64 == 0, (H + 2 n_kv) d %% 128 == 0 and q/k strides of the output views");
+  if (!x || !w_qkv || !qkv_out || !aligned(x, 16) || !aligned(w_qkv, 16) || !aligned(qkv_out, 16))
+    return fail(SSA_ERR_INVALID, "x, w_qkv and qkv_out must be non-null and 16-byte aligned");
+  if (!rand_proj || !aligned(rand_proj, 16)) return fail(SSA_ERR_INVALID, "rand_proj must be a 16-byte aligned fp32 array");
+  ssa::GraphDev g = dev_of(p);
+  const size_t need = ssa::graph_workspace_layout(&g);
+  if (!workspace || workspace_bytes < need)
+    return fail(SSA_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  g.ws = workspace;
+  ssa::graph_workspace_layout(&g);
+  const int n_out = (p->H + 2 * p->n_kv) * p->d;
+  g.q = qkv_out;
+  g.k = static_cast<const uint16_t*>(qkv_out) + (int64_t)p->H * p->d;
+  g.rp = rand_proj;
+  ssa::ProjDev pd;
+  pd.rows = p->B * p->N;
+  pd.dm = d_model;
+  pd.n_out = n_out;
+  pd.x = x;
+  pd.w = w_qkv;
+  pd.out = qkv_out;
+  cudaError_t e = ssa::launch_proj_hash(g, pd, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fused projection launch");
+  return SSA_OK;
+}
+
+int ssa_build_graph_prehashed(const ssa_graph_params* p, const void* q, const void* k, const float* rand_proj,
+                              const int32_t* glob, int32_t* nb_out, uint8_t* valid_out, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  return run_graph(p, q, k, rand_proj, glob, nb_out, valid_out, nullptr, workspace, workspace_bytes, stream, 0, 1);
 }
 
 int ssa_lsh_select(const ssa_graph_params* p, const void* q, const void* k, const float* rand_proj,

@@ -487,6 +487,7 @@ size_t graph_workspace_layout(GraphDev* g) {
     g->sample_s = s;
   }
   g->use_tc = select_tc_supported(*g) ? 1 : 0;
+  if (g->use_tc_hash) g->use_tc_hash = hash_tc_supported(*g) ? 1 : 0;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -500,9 +501,17 @@ size_t graph_workspace_layout(GraphDev* g) {
   const size_t o_pmax = take(sizeof(uint32_t) * BG * g->R);
   const int64_t ntq = (g->N + 127) / 128;
   const size_t o_flags = take((size_t)g->B * g->H * ntq);
+  const size_t o_hqc = take(2 * sizeof(unsigned int));
   const size_t o_zero_end = off;
   const size_t o_bsize = take(sizeof(int32_t) * BG * g->R * NB);
   const size_t o_lastc = take(sizeof(int32_t) * BG * g->R * NB);
+  size_t o_hpl = 0, o_pnorm = 0, o_hqk = 0, o_hqr = 0;
+  if (g->use_tc_hash) {
+    o_hpl = take(hash_tc_planes_bytes(*g));
+    o_pnorm = take(sizeof(float) * g->R * g->p);
+    o_hqk = take(sizeof(uint32_t) * BG * g->M * g->R);
+    o_hqr = take(sizeof(uint32_t) * rows * g->R);
+  }
   size_t o_qids = 0, o_qempty = 0, o_tau = 0, o_rcnt = 0, o_buf = 0, o_sspec = 0;
   if (g->use_tc) {
     o_qids = take(sizeof(uint16_t) * rows * g->NT);
@@ -521,6 +530,13 @@ size_t graph_workspace_layout(GraphDev* g) {
     g->tile_flags = reinterpret_cast<uint8_t*>(base + o_flags);
     g->bsize = reinterpret_cast<int32_t*>(base + o_bsize);
     g->lastc = reinterpret_cast<int32_t*>(base + o_lastc);
+    g->hq_count = reinterpret_cast<unsigned int*>(base + o_hqc);
+    if (g->use_tc_hash) {
+      g->hpl = reinterpret_cast<uint16_t*>(base + o_hpl);
+      g->pnorm = reinterpret_cast<float*>(base + o_pnorm);
+      g->hq_keys = reinterpret_cast<uint32_t*>(base + o_hqk);
+      g->hq_rows = reinterpret_cast<uint32_t*>(base + o_hqr);
+    }
     if (g->use_tc) {
       g->qids = reinterpret_cast<uint16_t*>(base + o_qids);
       g->qempty = reinterpret_cast<uint8_t*>(base + o_qempty);
@@ -584,12 +600,21 @@ static cudaError_t launch_select_dt(const GraphDev& g, int mode, int rows, size_
              : launch_select_t<DT, 128, uint32_t>(g, mode, rows, smem, st);
 }
 
-cudaError_t launch_graph(const GraphDev& g, int mode, cudaStream_t st) {
+cudaError_t launch_graph(const GraphDev& g_in, int mode, cudaStream_t st) {
   cudaError_t e;
+  GraphDev g = g_in;
+  if (!select_tc_pointers_ok(g)) g.use_tc_hash = 0;  // TMA needs 16-byte aligned rows
   stage_mark(kStageBegin, st);
-  e = cudaMemsetAsync(static_cast<char*>(g.ws) + g.zero_off, 0, g.zero_bytes, st);
-  if (e != cudaSuccess) return e;
-  {
+  if (g.prehashed) {
+    // ssa_qkv_proj_hash zeroed the workspace and wrote the key hash state.
+  } else if ((e = cudaMemsetAsync(static_cast<char*>(g.ws) + g.zero_off, 0, g.zero_bytes, st)) != cudaSuccess) {
+    return e;
+  }
+  if (g.prehashed) {
+  } else if (g.use_tc_hash) {
+    if ((e = launch_hash_planes(g, st)) != cudaSuccess) return e;
+    if ((e = launch_hash_tc(g, true, st)) != cudaSuccess) return e;
+  } else {
     const size_t planes = (size_t)g.R * g.p * g.d * sizeof(float);
     const bool smem = planes <= kHashPlaneSmemMax;
     const size_t sm = (smem ? planes : 0) + (size_t)8 * g.R * 32 * sizeof(uint16_t);

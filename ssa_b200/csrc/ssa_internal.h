@@ -41,6 +41,17 @@ struct GraphDev {
   unsigned long long* buf;        // [B*H*N][capg] kept (key << 32 | score bits); in the
                                   // sample pass kSampleTileBytes records per sampled tile
   uint8_t* tile_flags;            // [B*H][ceil(N/128)] tiles for the exact fallback
+  // tensor-core hash (bf16, head dim 64 / 128): keys always, queries with the
+  // tensor-core scan
+  int use_tc_hash;
+  float hash_eps;                 // c of the certification bound eps = c |x|_2 max_j |P[r][j]|_2
+  uint16_t* hpl;                  // hyperplane pieces in the B-operand layout (k_hash_planes)
+  float* pnorm;                   // [R][p] |P[r][j]|_2, rounded up
+  float* hash_dump;               // testing: tensor-core query projections [B*H*N][R][p], or null
+  int prehashed;                  // the hash state is already in the workspace (ssa_qkv_proj_hash)
+  unsigned int* hq_count;         // [2] flagged items queued: keys, queries (zeroed per build)
+  uint32_t* hq_keys;              // [BG*M*R] flagged (bg * M + key) << 4 | round
+  uint32_t* hq_rows;              // [B*H*N*R] flagged query row << 4 | round
   // outputs
   int32_t* lsh;                   // [B][H][N][A]
   int32_t* nb;                    // [B][H][N][Wout]
@@ -96,6 +107,24 @@ bool select_tc_supported(const GraphDev& g);
 bool select_tc_pointers_ok(const GraphDev& g);
 cudaError_t launch_select_tc(const GraphDev& g, int mode, cudaStream_t st);
 cudaError_t launch_hash_queries(const GraphDev& g, cudaStream_t st);
+bool hash_tc_supported(const GraphDev& g);
+size_t hash_tc_planes_bytes(const GraphDev& g);
+cudaError_t launch_hash_planes(const GraphDev& g, cudaStream_t st);
+cudaError_t launch_hash_tc(const GraphDev& g, bool keys, cudaStream_t st);
+int read_hash_tc_error(int clear);
+// Fused QKV projection + hash (self-attention, bf16): out[rows][n_out] =
+// x[rows][dm] w[n_out][dm]^T, with the graph's hash state written into its
+// workspace (g.q / g.k are views of out).
+struct ProjDev {
+  int rows, dm, n_out;
+  const void* x;
+  const void* w;
+  void* out;
+};
+bool proj_hash_supported(const GraphDev& g, int dm);
+cudaError_t launch_proj_hash(const GraphDev& g, const ProjDev& pd, cudaStream_t st);
+cudaError_t launch_qempty(const GraphDev& g, cudaStream_t st);
+unsigned long long read_hash_recomputed(int clear);
 cudaError_t launch_rows(const GraphDev& g, int stage, int mode, cudaStream_t st);
 size_t rows_smem_bytes(const GraphDev& g, int warps);
 int read_device_error(int clear);

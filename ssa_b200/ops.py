@@ -91,6 +91,77 @@ def _graph_inputs(q, k, rand_proj, glob):
     return q, (qsb, qsh, qsn), k, (ksb, ksh, ksm), rp, g
 
 
+class PrehashedGraph:
+    """The graph-build state a fused QKV projection leaves behind
+    (ssa_qkv_proj_hash): its params, the workspace holding the hash state,
+    the hyperplanes and the global indices, for build_graph_prehashed."""
+
+    def __init__(self, params, ws, rand_proj, glob):
+        self.params, self.ws, self.rand_proj, self.glob = params, ws, rand_proj, glob
+
+
+def qkv_project_hash(x: torch.Tensor, w_qkv: torch.Tensor, rand_proj: torch.Tensor, glob: torch.Tensor, *,
+                     H: int, n_kv: int, R: int, max_p: int, p_eff: int, C: int, T: int, A: int,
+                     causal: bool, K: int, window: int):
+    """Fused QKV projection + LSH hash (ssa_qkv_proj_hash): qkv = x w_qkv^T
+    as (B, N, (H + 2 n_kv) d) bf16 with w_qkv = [Wq; Wk; Wv], and the hash
+    state of the self-attention graph over its q / k views. Returns
+    (qkv, PrehashedGraph), or None when the fused path does not serve these
+    shapes (ssa_qkv_proj_hash_supported)."""
+    _require_cuda(x, w_qkv, rand_proj, glob)
+    if x.dim() != 3 or w_qkv.dim() != 2 or x.dtype != torch.bfloat16 or w_qkv.dtype != torch.bfloat16:
+        return None
+    B, N, dm = x.shape
+    n_out = w_qkv.shape[0]
+    if w_qkv.shape[1] != dm or n_out % (H + 2 * n_kv):
+        raise ValueError(f"w_qkv {tuple(w_qkv.shape)} does not match x {tuple(x.shape)} and the heads")
+    d = n_out // (H + 2 * n_kv)
+    x = x.contiguous()
+    w = w_qkv.contiguous()
+    qkv = torch.empty((B, N, n_out), dtype=torch.bfloat16, device=x.device)
+    q, k, _ = split_qkv(qkv, H, n_kv)
+    rp = rand_proj.detach().to(torch.float32).contiguous()
+    g = glob.to(torch.int32).contiguous() if glob is not None else None
+    p = graph_params(q, k, R=R, max_p=max_p, p_eff=p_eff, C=C, T=T, A=A, causal=causal, is_cross=False,
+                     K=K, window=window, G=g.numel() if g is not None else 0)
+    p.q_sb, p.q_sh, p.q_sn = q.stride()[:3]
+    p.k_sb, p.k_sh, p.k_sm = k.stride()[:3]
+    L = _lib.load()
+    if not L.ssa_qkv_proj_hash_supported(ctypes.byref(p), dm):
+        return None
+    ws_bytes = L.ssa_graph_workspace_size(ctypes.byref(p))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+    check(L.ssa_qkv_proj_hash(ctypes.byref(p), dm, _ptr(x), _ptr(w), _ptr(qkv), _ptr(rp), _ptr(ws), ws_bytes,
+                              _stream(x.device)), "ssa_qkv_proj_hash")
+    return qkv, PrehashedGraph(p, ws, rp, g)
+
+
+def split_qkv(qkv: torch.Tensor, H: int, n_kv: int):
+    """(B, N, (H + 2 n_kv) d) -> q (B, H, N, d), k, v (B, n_kv, N, d) views."""
+    B, N, n_out = qkv.shape
+    d = n_out // (H + 2 * n_kv)
+    q = qkv[..., :H * d].view(B, N, H, d).transpose(1, 2)
+    k = qkv[..., H * d:(H + n_kv) * d].view(B, N, n_kv, d).transpose(1, 2)
+    v = qkv[..., (H + n_kv) * d:].view(B, N, n_kv, d).transpose(1, 2)
+    return q, k, v
+
+
+def build_graph_prehashed(q: torch.Tensor, k: torch.Tensor, state: PrehashedGraph):
+    """ssa_build_graph_prehashed: the graph of the q / k views of a fused
+    projection's output, from the hash state it left; the same result as
+    build_graph on those views. Returns int32 neighbors and uint8 valid."""
+    p, ws = state.params, state.ws
+    L = _lib.load()
+    W = L.ssa_graph_width(ctypes.byref(p))
+    B, H, N = q.shape[:3]
+    nb = torch.empty((B, H, N, W), dtype=torch.int32, device=q.device)
+    valid = torch.empty((B, H, N, W), dtype=torch.uint8, device=q.device)
+    check(L.ssa_build_graph_prehashed(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(state.rand_proj), _ptr(state.glob),
+                                      _ptr(nb), _ptr(valid), _ptr(ws), ws.numel(), _stream(q.device)),
+          "ssa_build_graph_prehashed")
+    return nb, valid
+
+
 def build_graph(q: torch.Tensor, k: torch.Tensor, rand_proj: torch.Tensor, glob: torch.Tensor, *,
                 R: int, max_p: int, p_eff: int, C: int, T: int, A: int, causal: bool,
                 is_cross: bool, K: int, window: int, want_lsh: bool = False, q_row0: int = 0):

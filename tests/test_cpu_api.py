@@ -115,7 +115,7 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(L, n), n
     assert set(names) == set(_lib.SIGNATURES), "ctypes signatures out of sync with the header"
-    assert L.ssa_abi_version() == 105
+    assert L.ssa_abi_version() == 106
 
 
 def test_static_scratch_size_matches_header():
