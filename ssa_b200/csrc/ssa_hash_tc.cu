@@ -560,29 +560,32 @@ __global__ void __launch_bounds__(htc::hash_threads(NG), NG == 2 ? 2 : 1)
 // Fused QKV projection + hash
 // ---------------------------------------------------------------------------
 // out = x W^T for W = [Wq; Wk; Wv] (the projections feeding the graph build,
-// sparse_attention.py:1484-1486), bf16 with fp32 accumulation, in 128 x 128
-// tiles (one head at head dim 128, two at 64), persistent CTAs taking tiles
-// column-fastest (a row block of x stays in L2 while W streams from L2):
+// sparse_attention.py:1484-1486), bf16 with fp32 accumulation, in 128 x 256
+// tiles, persistent CTAs taking tiles column-fastest (a row block of x stays
+// in L2 while W streams from L2):
 //
-//   warp 8 (one lane)  TMA: the hyperplane pieces once, then 64-wide K slices
-//                      of the x and W tiles into a ring.
-//   warp 9             tcgen05.mma 128 x 128 x 16 into one of two TMEM
-//                      accumulators (columns 0-255); commits free ring slots.
-//   warps 0-7          two groups alternating tiles: the accumulator rounded
-//                      to bf16 into a staging tile (SWIZZLE_128B, K-major --
-//                      both the TMA-store source and the hash MMA's A
-//                      operand), one TMA store of the tile, then for each q /
-//                      k head of the tile the hash MMA (issued by the group's
-//                      first thread into TMEM columns 256 + group * NP) and
-//                      hash_rows: query slots, or key codes / member masks /
-//                      pad keys. qempty is left to the graph build (the bucket
-//                      sizes need every key).
+//   warp 4 (one lane)  TMA: the hyperplane pieces once, then 64-wide K slices
+//                      of the x (128 rows) and W (256 rows) tiles into a ring.
+//   warp 5             tcgen05.mma 128 x 256 x 16 into one of two TMEM
+//                      accumulators (256 columns each); commits free ring
+//                      slots and publish finished tiles.
+//   warps 0-3          thread per row, head by head: the head's columns
+//                      rounded to bf16 into a staging tile (SWIZZLE_128B,
+//                      K-major: the TMA-store source and the hash MMA's A
+//                      operand), one TMA store, and for a q or k head the
+//                      hash MMA -- issued by thread 0 into the head's
+//                      just-drained accumulator columns -- then hash_rows:
+//                      query slots, or key codes / member masks / pad keys.
+//                      qempty is left to the graph build (it needs the bucket
+//                      sizes of every key).
+// The epilogue of tile i overlaps the mainloop of tile i + 1.
 namespace prj {
-constexpr int TN = 128;  // tile columns
+constexpr int TN = 256;        // tile columns (MMA N)
+constexpr int THREADS = 192;   // warps 0-3 epilogue, 4 TMA, 5 MMA
+constexpr uint32_t kStage = (128 + TN) * 128;  // x 128 x 64 + W 256 x 64 bf16
 struct Plan {
-  uint32_t pl, ring, stg, pn, blk, bars, tmem_slot, total;
+  uint32_t pl, ring, stg, pn, bars, tmem_slot, total;
   int stages, np;
-  bool blk_on;
 };
 __host__ __device__ inline Plan plan(int D, const GraphDev& g) {
   Plan p;
@@ -595,17 +598,14 @@ __host__ __device__ inline Plan plan(int D, const GraphDev& g) {
   };
   p.np = htc::n_cols(g.R, g.p);
   p.pl = take(htc::planes_bytes(D, g.R, g.p), 1024);
-  const uint32_t blk = (uint32_t)g.R * (uint32_t)g.NB * 16u;
-  p.blk_on = blk <= htc::kBlkMax;
-  const uint32_t fixed = 2u * htc::ROWS * TN * 2 + htc::kMaxR * 4 + (p.blk_on ? 2u * blk : 0u) + 32 * 8 + 16 + 4096;
-  int st = 6;
-  while (st > 2 && off + (uint32_t)st * 32768u + fixed > 227u * 1024u) --st;
+  p.stg = take((uint32_t)htc::ROWS * D * 2, 1024);  // one head: D / 64 atoms of 128 x 64
+  const uint32_t tail = htc::kMaxR * 4 + 24 * 8 + 16 + 1024 + 64;
+  int st = 4;
+  while (st > 2 && ((off + 1023) / 1024 * 1024) + (uint32_t)st * kStage + tail > 227u * 1024u) --st;
   p.stages = st;
-  p.ring = take((uint32_t)st * 32768u, 1024);  // [stage] x tile 128 x 64, then W tile 128 x 64
-  p.stg = take(2u * htc::ROWS * TN * 2, 1024);  // [group] 128 x 128 bf16, two 64-column atoms
+  p.ring = take((uint32_t)st * kStage, 1024);
   p.pn = take(htc::kMaxR * 4, 16);
-  p.blk = take(p.blk_on ? 2u * blk : 0u, 16);
-  p.bars = take(32 * 8, 8);
+  p.bars = take(24 * 8, 8);
   p.tmem_slot = take(16, 16);
   p.total = off + 1024;
   return p;
@@ -613,7 +613,7 @@ __host__ __device__ inline Plan plan(int D, const GraphDev& g) {
 }  // namespace prj
 
 template <int D, int RC>
-__global__ void __launch_bounds__(htc::THREADS, 1)
+__global__ void __launch_bounds__(prj::THREADS, 1)
     k_proj_hash(GraphDev g, ProjDev pd, const __grid_constant__ CUtensorMap xmap,
                 const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap omap) {
   using namespace tc;
@@ -628,20 +628,22 @@ __global__ void __launch_bounds__(htc::THREADS, 1)
   const uint32_t idesc_h = idesc_bf16(ROWS, NP);
   unsigned char* pls = smem + sp.pl;
   unsigned char* ring = smem + sp.ring;
+  unsigned char* stg = smem + sp.stg;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + sp.bars);
   uint64_t* sfull = bars;          // [NS] K slice loaded (TMA tx)
-  uint64_t* sfree = bars + 6;      // [NS] K slice consumed (MMA commit)
-  uint64_t* afull = bars + 12;     // [2] tile accumulator ready
-  uint64_t* afree = bars + 14;     // [2] tile accumulator drained (the group's 4 warps)
-  uint64_t* hfull = bars + 16;     // [2] hash projections ready (the group's MMA commit)
-  uint64_t* pfull = bars + 18;     // hyperplane pieces loaded
-  uint64_t* mma_done = bars + 19;  // every mainloop MMA has completed
-  uint64_t* hdone = bars + 20;     // [2] every hash MMA of the group has completed
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 22);
+  uint64_t* sfree = bars + 4;      // [NS] K slice consumed (MMA commit)
+  uint64_t* afull = bars + 8;      // [2] tile accumulator ready
+  uint64_t* afree = bars + 10;     // [2] tile accumulator drained (the 4 epilogue warps)
+  uint64_t* hfull = bars + 12;     // hash projections ready (thread 0's commit)
+  uint64_t* pfull = bars + 13;     // hyperplane pieces loaded
+  uint64_t* mma_done = bars + 14;  // every mainloop MMA has completed
+  uint64_t* hdone = bars + 15;     // every hash MMA has completed
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 16);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + sp.tmem_slot);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ncol = pd.n_out / prj::TN;
+  const int ncol = (pd.n_out + prj::TN - 1) / prj::TN;
+  const int nheads = g.H + 2 * g.n_kv;
   const int64_t ntiles = (int64_t)(pd.rows / ROWS) * ncol;
   const int ntl = blockIdx.x < ntiles ? (int)((ntiles - 1 - blockIdx.x) / gridDim.x) + 1 : 0;
   const int nk = pd.dm / 64;
@@ -654,15 +656,15 @@ __global__ void __launch_bounds__(htc::THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(afull + i, 1);
       mbar_init(afree + i, 4);
-      mbar_init(hfull + i, 1);
-      mbar_init(hdone + i, 1);
     }
+    mbar_init(hfull, 1);
     mbar_init(pfull, 1);
     mbar_init(mma_done, 1);
+    mbar_init(hdone, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 9) {  // 2 x 128 accumulator columns + 2 x NP hash columns
+  if (warp == 5) {  // two 256-column accumulators
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
                  "r"(512));
@@ -673,7 +675,7 @@ __global__ void __launch_bounds__(htc::THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
+  if (warp == 4) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && ntl > 0) {
       const uint32_t pbytes = planes_bytes(D, g.R, g.p);
@@ -690,10 +692,11 @@ __global__ void __launch_bounds__(htc::THREADS, 1)
             stop = true;
             break;
           }
-          unsigned char* st = ring + (size_t)s * 32768;
-          mbar_expect_tx(sfull + s, 32768);
+          unsigned char* st = ring + (size_t)s * prj::kStage;
+          mbar_expect_tx(sfull + s, prj::kStage);
           tma_load_2d(st, &xmap, sfull + s, kc * 64, row0);
-          tma_load_2d(st + 16384, &wmap, sfull + s, kc * 64, col0);
+          tma_load_2d(st + 16384, &wmap, sfull + s, kc * 64, col0);  // W rows col0 .. +127
+          tma_load_2d(st + 32768, &wmap, sfull + s, kc * 64, col0 + 128);  // +128 .. +255 (zero past n_out)
           issued = c + 1;
         }
       }
@@ -701,7 +704,7 @@ __global__ void __launch_bounds__(htc::THREADS, 1)
       for (int64_t q = issued - NS > 0 ? issued - NS : 0; q < issued; ++q)
         mbar_drain(sfull + q % NS, (uint32_t)((q / NS) & 1));
     }
-  } else if (warp == 9) {
+  } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && ntl > 0) {
       int64_t c = 0;
@@ -718,7 +721,7 @@ __global__ void __launch_bounds__(htc::THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t xa = smem_u32(ring + (size_t)s * 32768), wa = xa + 16384;
+          const uint32_t xa = smem_u32(ring + (size_t)s * prj::kStage), wa = xa + 16384;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             umma_bf16(tmem + ab * prj::TN, umma_desc(xa + kk * 32), umma_desc(wa + kk * 32), idesc_g,
@@ -736,83 +739,76 @@ __global__ void __launch_bounds__(htc::THREADS, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    const int grp = warp >> 2, wq = warp & 3;
-    const int t = wq * 32 + lane;
-    const int bar_id = 1 + grp;
-    unsigned char* stg = smem + sp.stg + (size_t)grp * ROWS * prj::TN * 2;
+    const int t = threadIdx.x;  // row of the tile (TMEM lane)
+    const int bar_id = 1;
     float* s_pn = reinterpret_cast<float*>(smem + sp.pn);
-    const int nblk = g.R * g.NB;
-    uint4* blk = reinterpret_cast<uint4*>(smem + sp.blk) + grp * nblk;
-    if (sp.blk_on)
-      for (int e = t; e < nblk; e += ROWS) blk[e] = make_uint4(0u, 0u, 0u, 0u);
-    if (threadIdx.x < g.R) {
+    if (t < g.R) {
       float m = 0.f;
-      for (int j = 0; j < g.p; ++j) m = fmaxf(m, __ldg(g.pnorm + threadIdx.x * g.p + j));
-      s_pn[threadIdx.x] = m;
+      for (int j = 0; j < g.p; ++j) m = fmaxf(m, __ldg(g.pnorm + t * g.p + j));
+      s_pn[t] = m;
     }
     const bool planes_ok = ntl == 0 || mbar_wait_warp(pfull, 0, abort_flag, 34, g.wait_limit);
-    asm volatile("bar.sync 3, 256;" ::: "memory");  // both groups: s_pn, cleared blocks
-    const uint32_t hcol = tmem + 2 * prj::TN + (uint32_t)(grp * NP);
-    const uint32_t lrow = (uint32_t)(wq * 32) << 16;
-    int nh = 0;  // hash MMAs this group has issued (hfull phase)
+    group_sync(bar_id);
+    const uint32_t lrow = (uint32_t)(warp * 32) << 16;
+    int nh = 0;  // hash MMAs issued (hfull phase)
     bool stored = false;
-    for (int i = grp; i < ntl && planes_ok; i += 2) {
+    for (int i = 0; i < ntl && planes_ok; ++i) {
       const int64_t T = blockIdx.x + (int64_t)i * gridDim.x;
       const int row0 = (int)(T / ncol) * ROWS, col0 = (int)(T % ncol) * prj::TN;
       const int ab = i & 1;
       const bool ok = mbar_wait_warp(afull + ab, (i >> 1) & 1, abort_flag, 35, g.wait_limit);
       if (group_any(!ok, bar_id)) break;
       tc_fence_after();
-      // The previous tile's TMA store has read the staging tile.
-      if (t == 0 && stored) bulk_wait_read();
-      group_sync(bar_id);
-      // Accumulator -> bf16 (round to nearest) -> staging tile (row t: atom
-      // a at a * 16 KB, 16-byte chunk c at (c ^ (t & 7)) * 16), and the
-      // squared norm of the row's bf16 values per head.
-      float nrm2[prj::TN / D];
-#pragma unroll
-      for (int hh = 0; hh < prj::TN / D; ++hh) nrm2[hh] = 0.f;
-#pragma unroll
-      for (int cc = 0; cc < prj::TN / 32; ++cc) {
-        float f[32];
-        tmem_ld32(tmem + lrow + ab * prj::TN + cc * 32, f);
-        tmem_wait_ld();
-        uint32_t w[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const __nv_bfloat162 b2 = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
-          w[e] = *reinterpret_cast<const uint32_t*>(&b2);
-          const float lo = __uint_as_float(w[e] << 16), hi = __uint_as_float(w[e] & 0xFFFF0000u);
-          nrm2[(cc * 32) / D] = fmaf(lo, lo, fmaf(hi, hi, nrm2[(cc * 32) / D]));
-        }
-        unsigned char* rowp = stg + (cc >> 1) * (ROWS * 128) + t * 128;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int ch = (cc & 1) * 4 + u;
-          *reinterpret_cast<uint4*>(rowp + ((ch ^ (t & 7)) << 4)) =
-              make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(afree + ab);
-      fence_async_smem();
-      group_sync(bar_id);
-      if (t == 0) {
-#pragma unroll
-        for (int a = 0; a < prj::TN / 64; ++a) tma_store_2d(&omap, stg + a * ROWS * 128, col0 + a * 64, row0);
-        bulk_commit();
-        stored = true;
-      }
-      // Hash the q and k heads of the tile (N % 128 == 0: one batch element).
-      const int b = row0 / g.N, n0 = row0 % g.N;
+      const uint32_t acc = tmem + lrow + (uint32_t)(ab * prj::TN);
+      const int b = row0 / g.N, n0 = row0 % g.N;  // N % 128 == 0: one batch element per tile
+      bool aborted = false;
       for (int hh = 0; hh < prj::TN / D; ++hh) {
         const int hd = (col0 + hh * D) / D;
-        if (hd >= g.H + g.n_kv) continue;  // a v head
+        if (hd >= nheads) break;  // past the last head (uniform)
+        // The previous TMA store has read the staging tile.
+        if (t == 0 && stored) bulk_wait_read();
+        group_sync(bar_id);
+        // Head columns -> bf16 (round to nearest) -> staging (row t: atom a at
+        // a * 16 KB, 16-byte chunk c at (c ^ (t & 7)) * 16), and the squared
+        // norm of the row's bf16 values.
+        float nrm2 = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) {
+          float f[32];
+          tmem_ld32(acc + hh * D + cc * 32, f);
+          tmem_wait_ld();
+          uint32_t w[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const __nv_bfloat162 b2 = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
+            w[e] = *reinterpret_cast<const uint32_t*>(&b2);
+            const float lo = __uint_as_float(w[e] << 16), hi = __uint_as_float(w[e] & 0xFFFF0000u);
+            nrm2 = fmaf(lo, lo, fmaf(hi, hi, nrm2));
+          }
+          unsigned char* rowp = stg + (cc >> 1) * (ROWS * 128) + t * 128;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int ch = (cc & 1) * 4 + u;
+            *reinterpret_cast<uint4*>(rowp + ((ch ^ (t & 7)) << 4)) =
+                make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+          }
+        }
+        tc_fence_before();
+        fence_async_smem();
+        group_sync(bar_id);
+        if (t == 0) {
+#pragma unroll
+          for (int a = 0; a < KB; ++a) tma_store_2d(&omap, stg + a * ROWS * 128, col0 + hh * D + a * 64, row0);
+          bulk_commit();
+          stored = true;
+        }
+        if (hd >= g.H + g.n_kv) continue;  // a v head: no hash
         const bool key = hd >= g.H;
+        // Hash MMA into the head's drained accumulator columns (NP <= D).
+        const uint32_t hcol = tmem + (uint32_t)(ab * prj::TN + hh * D);
         if (t == 0) {
           tc_fence_after();
-          const uint32_t xa = smem_u32(stg + hh * KB * ROWS * 128), pa = smem_u32(pls);
+          const uint32_t xa = smem_u32(stg), pa = smem_u32(pls);
 #pragma unroll
           for (int c = 0; c < kPieces; ++c)
 #pragma unroll
@@ -821,22 +817,25 @@ __global__ void __launch_bounds__(htc::THREADS, 1)
               const uint32_t offb = (uint32_t)(c * KB + (kk >> 2)) * (uint32_t)NP * 128u + (kk & 3) * 32;
               umma_bf16(hcol, umma_desc(xa + offa), umma_desc(pa + offb), idesc_h, (c | kk) != 0);
             }
-          umma_commit(hfull + grp);
+          umma_commit(hfull);
         }
-        const bool hok = mbar_wait_warp(hfull + grp, nh & 1, abort_flag, 36, g.wait_limit);
+        const bool hok = mbar_wait_warp(hfull, nh & 1, abort_flag, 36, g.wait_limit);
         ++nh;
-        if (group_any(!hok, bar_id)) break;
+        if (group_any(!hok, bar_id)) {
+          aborted = true;
+          break;
+        }
         tc_fence_after();
         HashRow hr;
         hr.s_pn = s_pn;
-        hr.xn = sqrtf(nrm2[hh]) * (1.f + 1.f / 4096.f);
+        hr.xn = sqrtf(nrm2) * (1.f + 1.f / 4096.f);
         hr.act = true;
         hr.n = n0 + t;
         hr.r0 = n0;
         hr.lane = lane;
-        hr.wq = wq;
-        hr.blk = blk;
-        hr.blk_on = key && sp.blk_on;
+        hr.wq = warp;
+        hr.blk = nullptr;
+        hr.blk_on = false;
         hr.with_empty = false;
         hr.dump = nullptr;
         float v[32];
@@ -850,21 +849,22 @@ __global__ void __launch_bounds__(htc::THREADS, 1)
           hash_rows<false, RC, 32>(g, hr, hcol + lrow, NP, v, false);
         }
         tc_fence_before();
-        if (hr.blk_on) store_mask_block(g, blk, hr.bg, n0, t, bar_id);
-        else group_sync(bar_id);  // every row has read the hash columns before the next hash MMA
       }
+      if (aborted) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(afree + ab);  // every column of the accumulator has been read
     }
     if (t == 0) {
       if (stored) bulk_wait_all();
-      if (nh) {  // the group's hash MMAs have completed before TMEM is freed
-        umma_commit(hdone + grp);
-        mbar_drain(hdone + grp, 0);
+      if (nh) {  // the hash MMAs have completed before TMEM is freed
+        umma_commit(hdone);
+        mbar_drain(hdone, 0);
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 5) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
   }
@@ -1057,11 +1057,11 @@ cudaError_t launch_hash_tc(const GraphDev& g, bool keys, cudaStream_t st) {
 
 bool proj_hash_supported(const GraphDev& g, int dm) {
   if (!hash_tc_supported(g) || g.is_cross || g.M != g.N || g.N % 128 != 0) return false;
-  const int n_out = (g.H + 2 * g.n_kv) * g.d;
-  if (dm < 64 || dm % 64 != 0 || n_out % prj::TN != 0) return false;
+  if (dm < 64 || dm % 64 != 0) return false;
   if ((int64_t)g.B * g.N >= (int64_t(1) << 31)) return false;
   const prj::Plan sp = prj::plan(g.d, g);
-  if (sp.total > 227 * 1024 || 2 * prj::TN + 2 * sp.np > 512) return false;
+  // the hash accumulates in the head's drained accumulator columns
+  if (sp.total > 227 * 1024 || sp.np > g.d) return false;
   return true;
 }
 
@@ -1075,9 +1075,9 @@ static cudaError_t launch_proj_t(const GraphDev& g, const ProjDev& pd, cudaStrea
   auto fn = k_proj_hash<D, RC>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp.total);
   if (e != cudaSuccess) return e;
-  const int64_t ntiles = (int64_t)(pd.rows / htc::ROWS) * (pd.n_out / prj::TN);
+  const int64_t ntiles = (int64_t)(pd.rows / htc::ROWS) * ((pd.n_out + prj::TN - 1) / prj::TN);
   const int64_t grid = std::min<int64_t>(ntiles, sm_count());
-  fn<<<(unsigned)grid, htc::THREADS, sp.total, st>>>(g, pd, xmap, wmap, omap);
+  fn<<<(unsigned)grid, prj::THREADS, sp.total, st>>>(g, pd, xmap, wmap, omap);
   note_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   GraphDev f = g;

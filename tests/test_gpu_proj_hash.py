@@ -7,8 +7,9 @@ the unfused graph build.
   * the graph built from the fused kernel's hash state
     (ssa_build_graph_prehashed) equals ssa_build_graph on the q / k views of
     its output, bit for bit;
-  * SparseAttention uses the fused path for bf16 self-attention and its
-    output and gradients match the unfused module's within the bf16 band;
+  * SparseAttention with fuse_qkv set takes the fused path for bf16
+    self-attention, and its output and gradients match the unfused module's
+    within the bf16 band;
   * shapes the kernel does not serve are reported as such (None).
 """
 import zlib
@@ -28,7 +29,7 @@ pytestmark = pytest.mark.gpu
 CFGS = [
     ("gqa_d128", 2, 1024, 1024, 8, 2, 128, 16, 4, 8, 12, 0),
     ("mha_d64_probes2", 1, 2048, 512, 8, 8, 96, 8, 2, 8, 12, 2),
-    ("mqa_d64_r16", 2, 512, 768, 12, 1, 64, 4, 2, 16, 10, 1),
+    ("mqa_d64_probe1_partial_tile", 2, 512, 768, 12, 1, 64, 4, 2, 8, 12, 1),  # 896 output columns
 ]
 
 
