@@ -46,12 +46,14 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
-    ap.add_argument("--mode", default="fwd", choices=["fwd", "train", "model"],
+    ap.add_argument("--mode", default="fwd", choices=["fwd", "train", "model", "proj"],
                     help="fwd: graph build + attention forward (the headline metric); train: "
                          "graph build + attention forward + backward (one layer's attention core); "
                          "model: the training-config model step (c4: 6-layer SparseTransformer with "
                          "its vocab embedding, forward + out.sum().backward(), and the same with "
-                         "CachedGraphSparseTransformer(reuse_every=4) behind an embedding)")
+                         "CachedGraphSparseTransformer(reuse_every=4) behind an embedding); "
+                         "proj: the fused QKV projection + hash (ssa_qkv_proj_hash) and the graph "
+                         "built from it, against torch Linear + the graph build, from x")
     ap.add_argument("--impl", default="ssa", choices=["ssa", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -687,7 +689,7 @@ def run_e2e(args, job, dev, flush, world):
     on a third stream, so PCIe transfers overlap the kernels."""
     import torch
     import torch.distributed as dist
-    from ssa_b200.sharding import slice_views
+    from ssa_b200.sharding import GroupSlice, slice_views
     w, m = job.w, job.m
     stream = torch.cuda.current_stream(dev)
     s_in = torch.cuda.Stream(dev)
@@ -703,7 +705,15 @@ def run_e2e(args, job, dev, flush, world):
         if job.plan == "groups":
             views = [slice_views(job.q, job.k, job.v, s, rep) for s in job.slices]
         else:
-            views = [(job.q[b:b + 1], job.k[b:b + 1], job.v[b:b + 1]) for b in range(w.B)]
+            # At least eight chunks where the kv heads split evenly: a batch
+            # element's kv-head groups in equal parts (a shorter pipeline fill
+            # and drain than one chunk per batch element).
+            parts = 1
+            while w.B * parts < 8 and w.n_kv % (parts * 2) == 0:
+                parts *= 2
+            gp = w.n_kv // parts
+            views = [slice_views(job.q, job.k, job.v, GroupSlice(b, b + 1, g0, g0 + gp), rep)
+                     for b in range(w.B) for g0 in range(0, w.n_kv, gp)]
         chunks = [tuple(pin(t.transpose(1, 2)) for t in vw) for vw in views]      # (b, N|M, heads, d)
     outs_h = [torch.empty((c[0].shape[0], c[0].shape[1], w.H if job.plan == "rows" else c[0].shape[2], w.d),
                           dtype=job.q.dtype).pin_memory() for c in chunks]
@@ -829,12 +839,90 @@ def run_reference(args):
     return res
 
 
+def run_proj(args):
+    """QKV projection + graph build from the activations x, one GPU: the
+    fused tcgen05 projection whose epilogue hashes q and k
+    (ssa_qkv_proj_hash, then ssa_build_graph_prehashed) against torch
+    Linear (cuBLAS) + ssa_build_graph. Self-attention bf16 configs."""
+    import torch
+    from ssa_b200 import _lib, ops
+    from ssa_b200.workloads import WORKLOADS, make_module, make_x
+    w = WORKLOADS[args.workload]
+    if args.batch:
+        w = type(w)(**{**w.__dict__, "B": args.batch})
+    if w.cross or w.dtype != "bf16":
+        raise SystemExit("--mode proj is for bf16 self-attention configs (c2, c3)")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    m = make_module(w, dev)
+    x, _ = make_x(w, dev, seed=1)
+    W = torch.cat([m.Wq.weight, m.Wk.weight, m.Wv.weight]).detach()
+    lsh = m.lsh_builder
+    kw = dict(H=w.H, n_kv=w.n_kv, R=lsh.R, max_p=lsh.max_P, p_eff=lsh.compute_effective_p(w.N, lsh.C, lsh.max_P),
+              C=lsh.C, T=lsh.T, A=lsh.output_width(w.N, m.lsh_k), causal=w.causal, K=m.K, window=w.window)
+    glob = m._glob(w.N, dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def fused():
+        qkv, st = ops.qkv_project_hash(x, W, lsh.rand_proj, glob, **kw)
+        q, k, _ = ops.split_qkv(qkv, w.H, w.n_kv)
+        return ops.build_graph_prehashed(q, k, st)
+
+    def unfused():
+        qkv = torch.nn.functional.linear(x, W)
+        q, k, _ = ops.split_qkv(qkv, w.H, w.n_kv)
+        return m._graph(q, k, w.M, w.causal, False)
+
+    def timed(fn):
+        for _ in range(max(args.warmup, 0)):
+            fn()
+        torch.cuda.synchronize()
+        evs = []
+        for _ in range(args.steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        return statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+
+    with torch.no_grad():
+        if ops.qkv_project_hash(x, W, lsh.rand_proj, glob, **kw) is None:
+            raise SystemExit("the fused projection does not serve this config")
+        clocks = ClockSampler(0)
+        clocks.start()
+        launches0 = _lib.load().ssa_kernel_launches()
+        ms_f = timed(fused)
+        launches = (_lib.load().ssa_kernel_launches() - launches0) // max(args.steps + max(args.warmup, 0), 1)
+        ms_u = timed(unfused)
+        clk = clocks.stop()
+        nb_f, va_f = fused()
+        nb_u, va_u = unfused()
+        same = bool(torch.equal(va_f, va_u) and torch.equal(nb_f[va_u.bool()], nb_u[va_u.bool()]))
+    tokens = w.B * w.N
+    out = {"metric": "QKV projection + graph build tokens/s (fused tcgen05 projection + hash epilogue)",
+           "value": tokens / (ms_f / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": ms_f, "higher_is_better": True, "scaling": "strong",
+           "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic (seeded activations; random-init weights in reference order)",
+           "config": {**workload_config(w), "d_model": w.d_model},
+           "parallelism": "one GPU, whole job", "l2": "flushed (256 MB write) between timed steps",
+           "unfused_ms_per_step": ms_u, "unfused": "torch Linear (cuBLAS) + ssa_build_graph",
+           "graphs_equal": same, "gpu_launches_per_step": launches, "clocks": clk}
+    print(json.dumps(out))
+    return out
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         run_reference(args)
     elif args.mode == "model":
         run_model(args)
+    elif args.mode == "proj":
+        run_proj(args)
     else:
         run_gpu(args)
 
