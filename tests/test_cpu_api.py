@@ -204,6 +204,18 @@ def test_abi_validation_rejects_bad_arguments():
         _lib.check(_lib.SSA_ERR_UNSUPPORTED, "x")
 
 
+def test_fused_projection_rejects_unserved_params():
+    """ssa_qkv_proj_hash serves bf16 self-attention with the output-view
+    strides only; everything else is reported before any CUDA work."""
+    L = _lib.load()
+    fake = ctypes.c_void_p(0x1000)
+    for p in (_params(dtype=_lib.SSA_F32), _params(is_cross=1, causal=0), _params(q_sn=7)):
+        assert L.ssa_qkv_proj_hash_supported(ctypes.byref(p), 512) == 0
+        rc = L.ssa_qkv_proj_hash(ctypes.byref(p), 512, fake, fake, fake, fake, fake, 1 << 30, None)
+        assert rc == _lib.SSA_ERR_UNSUPPORTED, rc
+        assert "fused projection" in L.ssa_last_error().decode()
+
+
 def test_graph_width_matches_oracle_formula():
     from oracle import oracle as O
     L = _lib.load()
