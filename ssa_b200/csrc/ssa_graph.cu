@@ -521,6 +521,11 @@ size_t graph_workspace_layout(GraphDev* g) {
     o_sspec = take(sizeof(float) * rows * (g->R + 1));
     o_buf = take(sizeof(unsigned long long) * rows * g->capg);
   }
+  size_t o_qpc = 0, o_kpc = 0;
+  if (g->use_tc && g->dtype == kDtF32) {
+    o_qpc = take(sizeof(uint16_t) * 3 * rows * g->d);
+    o_kpc = take(sizeof(uint16_t) * 3 * BG * g->M * g->d);
+  }
   if (g->ws) {
     char* base = static_cast<char*>(g->ws);
     g->kcode = reinterpret_cast<uint16_t*>(base + o_kcode);
@@ -544,6 +549,10 @@ size_t graph_workspace_layout(GraphDev* g) {
       g->rcnt = reinterpret_cast<int32_t*>(base + o_rcnt);
       g->sspec = reinterpret_cast<float*>(base + o_sspec);
       g->buf = reinterpret_cast<unsigned long long*>(base + o_buf);
+      if (g->dtype == kDtF32) {
+        g->qpc = reinterpret_cast<uint16_t*>(base + o_qpc);
+        g->kpc = reinterpret_cast<uint16_t*>(base + o_kpc);
+      }
     }
     g->zero_off = o_zero_begin;
     g->zero_bytes = o_zero_end - o_zero_begin;

@@ -41,6 +41,8 @@ struct GraphDev {
   unsigned long long* buf;        // [B*H*N][capg] kept (key << 32 | score bits); in the
                                   // sample pass kSampleTileBytes records per sampled tile
   uint8_t* tile_flags;            // [B*H][ceil(N/128)] tiles for the exact fallback
+  uint16_t* qpc;                  // fp32 tensor-core scan: q as bf16 pieces [3*B][H][N][d]
+  uint16_t* kpc;                  //                        k as bf16 pieces [3*B][n_kv][M][d]
   // tensor-core hash (bf16, head dim 64 / 128): keys always, queries with the
   // tensor-core scan
   int use_tc_hash;

@@ -961,9 +961,12 @@ cudaError_t launch_rows(const GraphDev& g, int stage, int mode, cudaStream_t st)
   constexpr int kWarps = 4;
   const size_t sm = (size_t)kWarps * rows_warp_bytes(g, stage);
   if (sm > 227 * 1024) return cudaErrorInvalidConfiguration;
-  if (g.dtype != kDtBF16) return cudaErrorInvalidValue;  // the tensor-core path is bf16 only
+  // bf16 with head dim 64 / 128, fp32 with 64 (the tensor-core path)
+  const bool f32 = g.dtype == kDtF32;
+  if (f32 && g.d != 64) return cudaErrorInvalidValue;
   auto pick = [&](auto d64, auto d128) { return g.d <= 64 ? d64 : d128; };
-  auto fn = stage == 0 ? pick(k_rows<kDtBF16, 64, 0, 0>, k_rows<kDtBF16, 128, 0, 0>)
+  auto fn = f32 ? (stage == 0 ? k_rows<kDtF32, 64, 0, 0> : mode == 0 ? k_rows<kDtF32, 64, 1, 0> : k_rows<kDtF32, 64, 1, 1>)
+          : stage == 0 ? pick(k_rows<kDtBF16, 64, 0, 0>, k_rows<kDtBF16, 128, 0, 0>)
           : mode == 0  ? pick(k_rows<kDtBF16, 64, 1, 0>, k_rows<kDtBF16, 128, 1, 0>)
                        : pick(k_rows<kDtBF16, 64, 1, 1>, k_rows<kDtBF16, 128, 1, 1>);
   cudaError_t e;

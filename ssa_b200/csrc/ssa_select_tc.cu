@@ -25,6 +25,7 @@
 // Every wait on an mbarrier is bounded: on timeout the kernel records an
 // error code (ssa_device_error) and the pipeline drains and returns.
 #include <cuda.h>
+#include <cuda_bf16.h>
 
 #include "ssa_common.cuh"
 #include "ssa_internal.h"
@@ -54,7 +55,12 @@ __host__ __device__ inline uint32_t bm_tile_bytes(const GraphDev& g) {
   return (uint32_t)g.R * (uint32_t)g.NB * 16u;
 }
 
-__host__ __device__ inline SmemPlan plan_stages(int D, int NT, int stages, uint32_t bm_bytes, int bstages) {
+// fp32 inputs are scanned as three bf16 pieces per operand (x = hi + mid +
+// lo); bf16 inputs as themselves.
+__host__ __device__ inline int scan_pieces(const GraphDev& g) { return g.dtype == kDtF32 ? 3 : 1; }
+
+__host__ __device__ inline SmemPlan plan_stages(int D, int NT, int stages, uint32_t bm_bytes, int bstages,
+                                                int P) {
   SmemPlan p;
   uint32_t off = 0;
   auto take = [&](uint32_t bytes, uint32_t align) {
@@ -64,8 +70,8 @@ __host__ __device__ inline SmemPlan plan_stages(int D, int NT, int stages, uint3
     return o;
   };
   const uint32_t atoms = (uint32_t)D / 64;
-  p.q = take(atoms * ROWS * 128, 1024);
-  p.k = take((uint32_t)stages * atoms * NKEY * 128, 1024);
+  p.q = take((uint32_t)P * atoms * ROWS * 128, 1024);
+  p.k = take((uint32_t)stages * P * atoms * NKEY * 128, 1024);
   p.bm = take((uint32_t)bstages * bm_bytes, 128);
   p.toff = take((uint32_t)NT * ROWS * 2, 16);
   p.bars = take(24 * 8, 8);
@@ -83,17 +89,20 @@ __host__ __device__ inline SmemPlan plan_stages(int D, int NT, int stages, uint3
   return p;
 }
 
-// The deepest K ring (up to 4 stages) that keeps two CTAs per SM, with a
-// 3-stage (else 2-stage) ring of mask blocks when those are staged.
+// The deepest K ring (up to 4 stages) that keeps two CTAs per SM (one with
+// fp32 pieces), with a 3-stage (else 2-stage) ring of mask blocks when those
+// are staged.
 __host__ __device__ inline SmemPlan plan(int D, const GraphDev& g) {
   const uint32_t bmb = bm_tile_bytes(g);
   const bool staged = bmb <= 8192u;
+  const int P = scan_pieces(g);
+  const uint32_t budget = P == 1 ? 113 * 1024 : 227 * 1024;
   for (int bst = staged ? 3 : 0; bst >= (staged ? 2 : 0); --bst)
     for (int st = 4; st >= 2; --st) {
-      const SmemPlan p = plan_stages(D, g.NT, st, bmb, bst);
-      if (p.total <= 113 * 1024) return p;
+      const SmemPlan p = plan_stages(D, g.NT, st, bmb, bst, P);
+      if (p.total <= budget) return p;
     }
-  return plan_stages(D, g.NT, 2, bmb, 0);
+  return plan_stages(D, g.NT, 2, bmb, 0, P);
 }
 
 }  // namespace tc
@@ -104,8 +113,8 @@ __host__ __device__ inline SmemPlan plan(int D, const GraphDev& g) {
 // the half of the row's buffer that belongs to the tile's epilogue group.
 // rcnt[row][group] counts the candidates seen (pass 0) or kept (pass 1; above
 // half the buffer means overflow).
-template <int D, int PASS>
-__global__ void __launch_bounds__(tc::THREADS, 2)
+template <int D, int PASS, int P>
+__global__ void __launch_bounds__(tc::THREADS, P == 1 ? 2 : 1)
     k_scan_tc(GraphDev g, const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap) {
   using namespace tc;
   constexpr int pass = PASS;  // one instantiation per pass
@@ -177,17 +186,21 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
   if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      mbar_expect_tx(qfull, ATOMS * ROWS * 128);
-      for (int a = 0; a < ATOMS; ++a)
-        tma_load_4d(qs + a * ROWS * 128, &qmap, qfull, a * 64, h, n0, b);
+      // pieces c of q / k are batch entries c * B + b of the piece buffers
+      mbar_expect_tx(qfull, P * ATOMS * ROWS * 128);
+      for (int c = 0; c < P; ++c)
+        for (int a = 0; a < ATOMS; ++a)
+          tma_load_4d(qs + (c * ATOMS + a) * ROWS * 128, &qmap, qfull, a * 64, h, n0, c * g.B + b);
       int issued = 0, issued_b = 0;
       const unsigned long long* bmg = g.bmap + bmap_idx(g, bg, 0, 0, 0);
       for (int i = 0; i < ntl; ++i) {
         const int s = i % NS;
         if (!mbar_wait(kempty + s, ((i / NS) & 1) ^ 1, abort_flag, 11, g.wait_limit)) break;
-        mbar_expect_tx(kfull + s, ATOMS * NKEY * 128);
-        for (int a = 0; a < ATOMS; ++a)
-          tma_load_4d(ks + (s * ATOMS + a) * NKEY * 128, &kmap, kfull + s, a * 64, gk, i * step * NKEY, b);
+        mbar_expect_tx(kfull + s, P * ATOMS * NKEY * 128);
+        for (int c = 0; c < P; ++c)
+          for (int a = 0; a < ATOMS; ++a)
+            tma_load_4d(ks + ((s * P + c) * ATOMS + a) * NKEY * 128, &kmap, kfull + s, a * 64, gk,
+                        i * step * NKEY, c * g.B + b);
         issued = i + 1;
         if (NB_ST) {
           const int sb2 = i % NB_ST;
@@ -212,12 +225,22 @@ __global__ void __launch_bounds__(tc::THREADS, 2)
         if (!mbar_wait(kfull + s, (i / NS) & 1, abort_flag, 14, g.wait_limit)) break;
         if (!mbar_wait(sempty + sb, ((i >> 1) & 1) ^ 1, abort_flag, 15, g.wait_limit)) break;
         tc_fence_after();
-        const uint32_t ka = smem_u32(ks + s * ATOMS * NKEY * 128);
+        const uint32_t ka = smem_u32(ks + s * P * ATOMS * NKEY * 128);
+        // fp32: the six piece products down to 2^-16 relative (mid*mid,
+        // hi*lo, lo*hi, hi*mid, mid*hi, hi*hi; each bf16 product exact in
+        // fp32), smallest first; bf16: the one product.
+        constexpr int NPAIR = P == 1 ? 1 : 6;
+        constexpr int PA[6] = {1, 0, 2, 0, 1, 0}, PB[6] = {1, 2, 0, 1, 0, 0};
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (ROWS * 128) + (kk & 3) * 32;
-          const uint32_t offk = (kk >> 2) * (NKEY * 128) + (kk & 3) * 32;
-          umma_bf16(tmem + sb * NKEY, umma_desc(qa + off), umma_desc(ka + offk), kIdesc, kk > 0);
+        for (int pr = 0; pr < NPAIR; ++pr) {
+          const uint32_t qp = qa + (P == 1 ? 0 : PA[pr]) * ATOMS * ROWS * 128;
+          const uint32_t kp = ka + (P == 1 ? 0 : PB[pr]) * ATOMS * NKEY * 128;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (ROWS * 128) + (kk & 3) * 32;
+            const uint32_t offk = (kk >> 2) * (NKEY * 128) + (kk & 3) * 32;
+            umma_bf16(tmem + sb * NKEY, umma_desc(qp + off), umma_desc(kp + offk), kIdesc, (pr | kk) > 0);
+          }
         }
         umma_commit(kempty + s);
         umma_commit(sfull + sb);
@@ -455,30 +478,59 @@ bool tc_make_map(CUtensorMap* m, const void* base, int d, int heads, int rows, i
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// fp32 q / k as three bf16 pieces each (hi = rn(x), mid = rn(x - hi),
+// lo = rn(x - hi - mid)), in contiguous piece buffers [3 * B][heads][rows][d]
+// that the scan's TMA maps read (piece c of batch b at batch index c * B + b).
+__global__ void __launch_bounds__(256) k_split_pieces(const float* __restrict__ x, int B, int heads, int rows,
+                                                      int d, int64_t sb, int64_t sh, int64_t sn,
+                                                      uint16_t* __restrict__ out) {
+  const int64_t total = (int64_t)B * heads * rows * d;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i % d);
+    int64_t r = i / d;
+    const int n = (int)(r % rows);
+    r /= rows;
+    const int h = (int)(r % heads);
+    const int b = (int)(r / heads);
+    const float v = __ldg(x + b * sb + h * sh + n * sn + t);
+    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+    const float r1 = v - __bfloat162float(hi);
+    const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+    out[i] = __bfloat16_as_ushort(hi);
+    out[total + i] = __bfloat16_as_ushort(mid);
+    out[2 * total + i] = __bfloat16_as_ushort(lo);
+  }
+}
+
 bool select_tc_supported(const GraphDev& g) {
-  if (g.dtype != kDtBF16 || (g.d != 64 && g.d != 128)) return false;
+  // bf16 with head dim 64 / 128; fp32 (as bf16 pieces) with head dim 64
+  if (g.dtype == kDtBF16 ? (g.d != 64 && g.d != 128) : g.d != 64) return false;
   if (g.M > 65536 || g.A > 1024) return false;
   if ((int64_t)g.B * g.H * g.N >= (int64_t(1) << 31)) return false;  // 32-bit row indices in k_rows
   if (g.R + 2 + (g.G < g.C ? g.G : g.C) > 32) return false;  // one special key per lane
   // TMA: 16-byte aligned strides (the base pointers are checked at launch)
   auto al = [](int64_t s) { return (s * 2) % 16 == 0; };
-  if (!al(g.q_sh) || !al(g.q_sn) || !al(g.q_sb) || !al(g.k_sh) || !al(g.k_sm) || !al(g.k_sb)) return false;
+  if (g.dtype == kDtBF16 &&
+      (!al(g.q_sh) || !al(g.q_sn) || !al(g.q_sb) || !al(g.k_sh) || !al(g.k_sm) || !al(g.k_sb)))
+    return false;
   if ((int64_t)g.R * g.NB > 65535) return false;  // 16-bit mask-block offsets
   const tc::SmemPlan sp = tc::plan(g.d, g);
-  if (sp.total > 113 * 1024) return false;
+  if (sp.total > (tc::scan_pieces(g) == 1 ? 113u : 227u) * 1024) return false;
   if (rows_smem_bytes(g, 1) > 227 * 1024) return false;
   return tc_encode_available();
 }
 
 bool select_tc_pointers_ok(const GraphDev& g) {
+  if (g.dtype == kDtF32) return true;  // the scan reads the piece buffers in the workspace
   return (reinterpret_cast<uintptr_t>(g.q) % 16) == 0 && (reinterpret_cast<uintptr_t>(g.k) % 16) == 0;
 }
 
-template <int D>
+template <int D, int P>
 static cudaError_t launch_scan_t(const GraphDev& g, int pass, const CUtensorMap& qmap,
                                  const CUtensorMap& kmap, cudaStream_t st) {
   const tc::SmemPlan sp = tc::plan(D, g);
-  auto fn = pass == 0 ? k_scan_tc<D, 0> : k_scan_tc<D, 1>;
+  auto fn = pass == 0 ? k_scan_tc<D, 0, P> : k_scan_tc<D, 1, P>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp.total);
   if (e != cudaSuccess) return e;
   dim3 grid((g.N + tc::ROWS - 1) / tc::ROWS, g.B * g.H);
@@ -492,17 +544,35 @@ static cudaError_t launch_scan_t(const GraphDev& g, int pass, const CUtensorMap&
 // exact FMA scan (launch_graph).
 cudaError_t launch_select_tc(const GraphDev& g, int mode, cudaStream_t st) {
   CUtensorMap qmap, kmap;
-  // q (B, H, N, d): dims {d, H, N, B}; k (B, n_kv, M, d): dims {d, n_kv, M, B}
-  if (!tc_make_map(&qmap, g.q, g.d, g.H, g.N, g.B, g.q_sh, g.q_sn, g.q_sb)) return cudaErrorInvalidValue;
-  if (!tc_make_map(&kmap, g.k, g.d, g.n_kv, g.M, g.B, g.k_sh, g.k_sm, g.k_sb)) return cudaErrorInvalidValue;
   cudaError_t e;
+  if (g.dtype == kDtF32) {
+    // fp32: the scan reads bf16 pieces: (3 B, H, N, d) and (3 B, n_kv, M, d)
+    const int64_t nq = (int64_t)g.B * g.H * g.N * g.d, nk = (int64_t)g.B * g.n_kv * g.M * g.d;
+    k_split_pieces<<<(unsigned)std::min<int64_t>((nq + 255) / 256, 4096), 256, 0, st>>>(
+        static_cast<const float*>(g.q), g.B, g.H, g.N, g.d, g.q_sb, g.q_sh, g.q_sn, g.qpc);
+    note_launch();
+    k_split_pieces<<<(unsigned)std::min<int64_t>((nk + 255) / 256, 4096), 256, 0, st>>>(
+        static_cast<const float*>(g.k), g.B, g.n_kv, g.M, g.d, g.k_sb, g.k_sh, g.k_sm, g.kpc);
+    note_launch();
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if (!tc_make_map(&qmap, g.qpc, g.d, g.H, g.N, 3 * g.B, g.N * (int64_t)g.d, g.d, (int64_t)g.H * g.N * g.d) ||
+        !tc_make_map(&kmap, g.kpc, g.d, g.n_kv, g.M, 3 * g.B, g.M * (int64_t)g.d, g.d,
+                     (int64_t)g.n_kv * g.M * g.d))
+      return cudaErrorInvalidValue;
+  } else {
+    // q (B, H, N, d): dims {d, H, N, B}; k (B, n_kv, M, d): dims {d, n_kv, M, B}
+    if (!tc_make_map(&qmap, g.q, g.d, g.H, g.N, g.B, g.q_sh, g.q_sn, g.q_sb)) return cudaErrorInvalidValue;
+    if (!tc_make_map(&kmap, g.k, g.d, g.n_kv, g.M, g.B, g.k_sh, g.k_sm, g.k_sb)) return cudaErrorInvalidValue;
+  }
   // Query ids: hashed here, or already written by the fused projection
   // (then only qempty, which needs the bucket sizes).
   e = g.prehashed ? launch_qempty(g, st) : (g.use_tc_hash ? launch_hash_tc(g, false, st) : launch_hash_queries(g, st));
   if (e != cudaSuccess) return e;
   stage_mark(kStageHashQueries, st);
   for (int pass = 0; pass < 2; ++pass) {
-    e = g.d == 64 ? launch_scan_t<64>(g, pass, qmap, kmap, st) : launch_scan_t<128>(g, pass, qmap, kmap, st);
+    e = g.dtype == kDtF32 ? launch_scan_t<64, 3>(g, pass, qmap, kmap, st)
+        : g.d == 64       ? launch_scan_t<64, 1>(g, pass, qmap, kmap, st)
+                          : launch_scan_t<128, 1>(g, pass, qmap, kmap, st);
     if (e != cudaSuccess) return e;
     stage_mark(pass == 0 ? kStageScanSample : kStageScanFull, st);
     if ((e = launch_rows(g, pass, mode, st)) != cudaSuccess) return e;
