@@ -57,6 +57,8 @@ def parse_args(argv=None):
     ap.add_argument("--impl", default="ssa", choices=["ssa", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-chunks", type=int, default=8,
+                    help="e2e: at least this many pipeline chunks where the kv heads split evenly")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the workload's batch size (profiling a smaller case)")
     ap.add_argument("--shard", default="auto", choices=["auto", "groups", "rows"],
@@ -705,11 +707,11 @@ def run_e2e(args, job, dev, flush, world):
         if job.plan == "groups":
             views = [slice_views(job.q, job.k, job.v, s, rep) for s in job.slices]
         else:
-            # At least eight chunks where the kv heads split evenly: a batch
-            # element's kv-head groups in equal parts (a shorter pipeline fill
-            # and drain than one chunk per batch element).
+            # At least --e2e-chunks chunks where the kv heads split evenly: a
+            # batch element's kv-head groups in equal parts (a shorter
+            # pipeline fill and drain than one chunk per batch element).
             parts = 1
-            while w.B * parts < 8 and w.n_kv % (parts * 2) == 0:
+            while w.B * parts < args.e2e_chunks and w.n_kv % (parts * 2) == 0:
                 parts *= 2
             gp = w.n_kv // parts
             views = [slice_views(job.q, job.k, job.v, GroupSlice(b, b + 1, g0, g0 + gp), rep)

@@ -222,7 +222,7 @@ def merge_neighbors(win_idx: torch.Tensor, glob_idx: torch.Tensor, lsh_idx: torc
     padding (index 0, valid False). Returns int64 neighbors and bool valid."""
     nb, valid = ops.merge(win_idx.to(lsh_idx.device), glob_idx.to(lsh_idx.device), lsh_idx,
                           self_idx, total_k)
-    return nb.long(), valid.bool()
+    return nb.long(), valid.view(torch.bool)  # 0 / 1 bytes: a view, no copy
 
 
 # ---------------------------------------------------------------------------
@@ -379,7 +379,7 @@ class SparseAttention(nn.Module):
         """(neighbors int64, valid bool), both (B, H, N, K): window + global +
         LSH + self, merged and deduplicated."""
         nb, valid = self._graph(q, k, M, bool(causal) and not is_cross, is_cross)
-        return nb.long(), valid.bool()
+        return nb.long(), valid.view(torch.bool)  # 0 / 1 bytes: a view, no copy
 
     def apply_graph(self, q, k, v, neighbors, valid) -> torch.Tensor:
         return sparse_gather_attention(q, k, v, neighbors, scale=self.scale, valid=valid,
@@ -492,7 +492,7 @@ def measure_cross_layer_overlap(model: "SparseTransformer", x: torch.Tensor) -> 
         k = attn._split_kv_grouped(attn.Wk(normed))
         v = attn._split_kv_grouped(attn.Wv(normed))
         nb, valid = attn._graph(q, k, N, attn.config.causal, False)
-        graphs.append((nb.long(), valid.bool()))
+        graphs.append((nb.long(), valid.view(torch.bool)))
         out = ops.gather_attention(q, k, v, nb, valid, attn.scale, attn.config.fp32_attn_weights)
         a = attn.Wo(out.transpose(1, 2).reshape(B, N, attn.H * attn.d_head))
         h = h + a + layer.ff(layer.norm2(h + a))
