@@ -509,8 +509,10 @@ size_t graph_workspace_layout(GraphDev* g) {
   if (g->use_tc_hash) {
     o_hpl = take(hash_tc_planes_bytes(*g));
     o_pnorm = take(sizeof(float) * g->R * g->p);
-    o_hqk = take(sizeof(uint32_t) * BG * g->M * g->R);
-    o_hqr = take(sizeof(uint32_t) * rows * g->R);
+    // per-CTA segments of ceil(tiles / CTAs) tiles' items: below 2 x tiles x 128 x R
+    const int64_t tk = BG * ((g->M + 127) / 128), tq = (int64_t)g->B * g->H * ((g->N + 127) / 128);
+    o_hqk = take(sizeof(uint32_t) * 2 * tk * 128 * g->R);
+    o_hqr = take(sizeof(uint32_t) * 2 * tq * 128 * g->R);
   }
   size_t o_qids = 0, o_qempty = 0, o_tau = 0, o_rcnt = 0, o_buf = 0, o_sspec = 0;
   if (g->use_tc) {

@@ -100,7 +100,7 @@ __host__ __device__ inline Plan plan_stages(int D, const GraphDev& g, bool keys,
   p.np = n_cols(g.R, g.p);
   p.pl = take(planes_bytes(D, g.R, g.p), 1024);
   p.a = take((uint32_t)stages * (uint32_t)(D / 64) * ROWS * 128, 1024);
-  p.pn = take(kMaxR * 4, 16);                                         // [R] max_j |P[r][j]|_2
+  p.pn = take(kMaxR * 4 + 16, 16);                                    // [R] max_j |P[r][j]|_2, queue count
   const uint32_t blk = (uint32_t)g.R * (uint32_t)g.NB * 16u;
   p.blk_on = keys && blk <= kBlkMax;
   p.blk = take(p.blk_on ? (uint32_t)NG * blk : 0u, 16);                // [group][R][NB] 4 x u32
@@ -233,7 +233,12 @@ struct HashRow {
   bool blk_on;
   bool with_empty;         // queries: OR of the certified slots' empty buckets
   float* dump;             // testing: this row's projections, or null
+  uint32_t* gq;            // queue of flagged (row << 4 | round) items, and its counter
+  unsigned int* gcount;
 };
+
+template <int D, bool KEYS>
+__device__ void fixup_items(const GraphDev& g, const uint32_t* q, unsigned int count, int64_t gw, int64_t nw);
 
 // Projection columns in batches of BW (TMEM lane = row; round r at columns
 // RC r .. RC r + p - 1 of ta). Per round: sign bits, certification (every
@@ -249,8 +254,6 @@ __device__ __forceinline__ bool hash_rows(const GraphDev& g, const HashRow& c, u
   using namespace htc;
   const int Te = KEYS ? 0 : g.Te;
   const int64_t total = (int64_t)g.B * g.H * g.N;
-  uint32_t* gq = KEYS ? g.hq_keys : g.hq_rows;
-  unsigned int* gcount = g.hq_count + (KEYS ? 0 : 1);
   bool empty = false;
   auto round_ids = [&](const float* vr, int r) {
     const float eps = g.hash_eps * c.xn * c.s_pn[r];
@@ -290,7 +293,7 @@ __device__ __forceinline__ bool hash_rows(const GraphDev& g, const HashRow& c, u
         if (tt < Te) pid |= (uint32_t)best << (4 * tt);
       }
     }
-    if (c.act && bad) gq[atomicAdd(gcount, 1u)] = (c.rowid << 4) | (uint32_t)r;
+    if (c.act && bad) c.gq[atomicAdd(c.gcount, 1u)] = (c.rowid << 4) | (uint32_t)r;
     const bool cert = c.act && !bad;
     if constexpr (KEYS) {
       // as k_hash_keys: 32 consecutive keys per warp (a quarter of the
@@ -481,6 +484,12 @@ __global__ void __launch_bounds__(htc::hash_threads(NG), NG == 2 ? 2 : 1)
       for (int j = 0; j < g.p; ++j) m = fmaxf(m, __ldg(g.pnorm + threadIdx.x * g.p + j));
       s_pn[threadIdx.x] = m;
     }
+    // Flagged (row, round) items: this CTA's own segment of the queue (at most
+    // its tiles' rows x R items), recomputed by the epilogue after its tiles.
+    unsigned int* qcount = reinterpret_cast<unsigned int*>(s_pn + kMaxR);
+    const int64_t seg_cap = ((ntiles + gridDim.x - 1) / gridDim.x) * (int64_t)ROWS * g.R;
+    uint32_t* qseg = (KEYS ? g.hq_keys : g.hq_rows) + (int64_t)blockIdx.x * seg_cap;
+    if (threadIdx.x == 0) *qcount = 0u;
     asm volatile("bar.sync 5, %0;" ::"r"(NG * 128) : "memory");  // every group
     for (int i = grp; i < ntl; i += NG) {
       const int64_t T = blockIdx.x + (int64_t)i * gridDim.x;
@@ -540,13 +549,21 @@ __global__ void __launch_bounds__(htc::hash_threads(NG), NG == 2 ? 2 : 1)
       hr.blk_on = blk_on;
       hr.with_empty = true;
       hr.dump = (!KEYS && g.hash_dump && act) ? g.hash_dump + (int64_t)hr.rowid * g.R * g.p : nullptr;
+      hr.gq = qseg;
+      hr.gcount = qcount;
       const bool empty = hash_rows<KEYS, RC, BW>(g, hr, ta, NP, v, true);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(afree + ab);
-      if (!KEYS && act) g.qempty[hr.rowid] = empty ? 1 : 0;  // k_hash_fixup adds the flagged rounds
+      if (!KEYS && act) g.qempty[hr.rowid] = empty ? 1 : 0;  // the recompute below adds the flagged rounds
       if (blk_on) store_mask_block(g, blk, bg, r0, t, bar_id);
     }
+    // The flagged items of this CTA's tiles (whose mask blocks it has
+    // stored), eight per warp pass in the fp32 order of the FMA kernels.
+    asm volatile("bar.sync 5, %0;" ::"r"(NG * 128) : "memory");
+    const unsigned int nq = *qcount;
+    if (!*abort_flag) fixup_items<D, KEYS>(g, qseg, nq, warp, NG * 4);
+    if (threadIdx.x == 0 && nq) atomicAdd(&g_hash_recomputed, (unsigned long long)nq);
   }
   tc_fence_before();
   __syncthreads();
@@ -838,6 +855,8 @@ __global__ void __launch_bounds__(prj::THREADS, 1)
         hr.blk_on = false;
         hr.with_empty = false;
         hr.dump = nullptr;
+        hr.gq = key ? g.hq_keys : g.hq_rows;
+        hr.gcount = g.hq_count + (key ? 0 : 1);
         float v[32];
         if (key) {
           hr.bg = b * g.n_kv + (hd - g.H);
@@ -900,13 +919,8 @@ __global__ void __launch_bounds__(256) k_qempty(GraphDev g) {
 // hash kernel wrote qempty from the other rounds). Keys: kcode, the member
 // bit and the pad-key maximum -- after the hash kernel stored its mask blocks.
 template <int D, bool KEYS>
-__global__ void __launch_bounds__(256) k_hash_fixup(GraphDev g) {
-  const unsigned int count = g.hq_count[KEYS ? 0 : 1];
-  const uint32_t* q = KEYS ? g.hq_keys : g.hq_rows;
-  if (blockIdx.x == 0 && threadIdx.x == 0 && count) atomicAdd(&g_hash_recomputed, (unsigned long long)count);
+__device__ void fixup_items(const GraphDev& g, const uint32_t* q, unsigned int count, int64_t gw, int64_t nw) {
   const int lane = threadIdx.x & 31, sub = lane & 3;
-  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int Te = KEYS ? 0 : g.Te;
   const int64_t total = (int64_t)g.B * g.H * g.N;
   for (int64_t base = gw * 8; base < (int64_t)count; base += nw * 8) {
@@ -975,6 +989,15 @@ __global__ void __launch_bounds__(256) k_hash_fixup(GraphDev g) {
   }
 }
 
+// The fused projection's flagged items (one global queue per kind).
+template <int D, bool KEYS>
+__global__ void __launch_bounds__(256) k_hash_fixup(GraphDev g) {
+  const unsigned int count = g.hq_count[KEYS ? 0 : 1];
+  if (blockIdx.x == 0 && threadIdx.x == 0 && count) atomicAdd(&g_hash_recomputed, (unsigned long long)count);
+  fixup_items<D, KEYS>(g, KEYS ? g.hq_keys : g.hq_rows, count,
+                       ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5, ((int64_t)gridDim.x * blockDim.x) >> 5);
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -1035,9 +1058,6 @@ static cudaError_t launch_hash_tc_t(const GraphDev& g, cudaStream_t st) {
   const int64_t grid = std::min<int64_t>(ntiles, (int64_t)sm_count() * per_sm);
   if (grid <= 0) return cudaSuccess;
   fn<<<(unsigned)grid, threads, sp.total, st>>>(g, map);
-  note_launch();
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  k_hash_fixup<D, KEYS><<<2 * sm_count(), 256, 0, st>>>(g);
   note_launch();
   return cudaGetLastError();
 }

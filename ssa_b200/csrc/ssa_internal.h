@@ -51,9 +51,9 @@ struct GraphDev {
   float* pnorm;                   // [R][p] |P[r][j]|_2, rounded up
   float* hash_dump;               // testing: tensor-core query projections [B*H*N][R][p], or null
   int prehashed;                  // the hash state is already in the workspace (ssa_qkv_proj_hash)
-  unsigned int* hq_count;         // [2] flagged items queued: keys, queries (zeroed per build)
-  uint32_t* hq_keys;              // [BG*M*R] flagged (bg * M + key) << 4 | round
-  uint32_t* hq_rows;              // [B*H*N*R] flagged query row << 4 | round
+  unsigned int* hq_count;         // [2] fused projection: flagged items queued, keys / queries
+  uint32_t* hq_keys;              // flagged (bg * M + key) << 4 | round (per-CTA segments in k_hash_tc)
+  uint32_t* hq_rows;              // flagged query row << 4 | round
   // outputs
   int32_t* lsh;                   // [B][H][N][A]
   int32_t* nb;                    // [B][H][N][Wout]
