@@ -22,23 +22,28 @@
 //     in global memory (warp-cooperative, four lanes per item), bit-identical
 //     to the FMA kernels. So the ids equal the FMA kernels' everywhere.
 //
-// One persistent CTA per SM (two for head dim 64), 128-row tiles of one
-// (batch, head) slice, round-robin over the CTAs:
+// k_hash_tc: persistent CTAs (one per SM; two for head dim 64 when only two
+// epilogue groups fit), 128-row tiles of one (batch, head) slice, round-robin
+// over the CTAs:
 //
-//   warp 8 (one lane)  bulk-copies the hyperplane pieces once (an image in
-//                      the UMMA SWIZZLE_128B K-major layout that
-//                      k_hash_planes writes), then TMA-loads 128-row tiles
-//                      into a 2-4 stage ring.
-//   warp 9             allocates TMEM (two accumulators of 16 columns per
-//                      round) and issues the 3 * d / 16 MMAs of a tile
-//                      (M = 128, N = 16 R, K = 16).
-//   warps 0-7          two groups of four, alternating tiles; thread per row
-//                      (TMEM lane = row): row norm from the staged tile, ids
-//                      and certification per round, the exact recompute of
-//                      the flagged (row, round) items, then the outputs:
-//                      queries -- qids per (round, probe) slot and qempty;
-//                      keys -- kcode, the bucket member masks and pmax (as
-//                      k_hash_keys).
+//   TMA warp (one lane)  bulk-copies the hyperplane pieces once (an image in
+//                        the UMMA SWIZZLE_128B K-major layout that
+//                        k_hash_planes writes), then TMA-loads 128-row tiles
+//                        into a 2-4 stage ring.
+//   MMA warp             allocates TMEM (one accumulator per epilogue group,
+//                        8 or 16 columns per round) and issues the 3 * d / 16
+//                        MMAs of a tile (M = 128, N = 8 R or 16 R, K = 16).
+//   NG epilogue groups   four warps each, taking tiles in turn; thread per row
+//                        (TMEM lane = row): row norm from the staged tile, ids
+//                        and certification per round, then the outputs --
+//                        queries: qids per (round, probe) slot and qempty;
+//                        keys: kcode, the member-mask block and pmax (as
+//                        k_hash_keys). Uncertified (row, round) items go to
+//                        the CTA's own queue segment, which its epilogue
+//                        warps recompute after the CTA's last tile.
+//
+// k_proj_hash (further below) is the fused QKV projection whose epilogue
+// runs the same per-row hashing on its freshly rounded q / k tiles.
 //
 // Every wait on an mbarrier is bounded (GraphDev::wait_limit); a group
 // decides together (barrier vote) to stop when one of its waits ran out.
@@ -58,7 +63,6 @@ static __device__ unsigned long long g_hash_recomputed = 0ull;
 namespace htc {
 
 constexpr int ROWS = 128;      // rows per tile (MMA M, TMEM lanes)
-constexpr int THREADS = 320;   // fused projection: warps 0-7 epilogue (two groups), 8 TMA, 9 MMA
 // Hash kernel: NG epilogue groups of four warps, then the TMA and MMA warps.
 __host__ __device__ constexpr int hash_threads(int NG) { return 32 * (4 * NG + 2); }
 constexpr int kPieces = 3;     // bf16 pieces of an fp32 hyperplane element
