@@ -126,11 +126,15 @@ __global__ void __launch_bounds__(256) k_attn_fwd(AttnDev a) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   float sum = 0.f;
-  for (int j = lane; j < a.Kn; j += 32) sum += expf(s[j] - mx);
+  for (int j = lane; j < a.Kn; j += 32) {
+    const float e = expf(s[j] - mx);
+    s[j] = e;
+    sum += e;
+  }
 #pragma unroll
   for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   for (int j = lane; j < a.Kn; j += 32) {
-    float p = expf(s[j] - mx) / sum;
+    float p = s[j] / sum;
     if (DT == kDtBF16 && !FP32W) p = round_bf16(p);  // attn.to(v.dtype) (:1190)
     if (a.drop_thresh) {  // F.dropout(attn, p) (:1193-1194), in the weights' dtype
       const bool keep = dropout_keep((unsigned long long)row * a.Kn + j, a.drop_seed, a.drop_offset,
@@ -176,8 +180,9 @@ __global__ void __launch_bounds__(256) k_attn_fwd(AttnDev a) {
 // Forward, vectorised: used when every row slice is 16-byte aligned and the
 // head dim is exactly 8 * EPL. The row's slot keys (-1 for slots that take
 // no part) are staged in shared memory first, so no gather waits on an index
-// load; each lane moves its 32-byte (bf16) or 64-byte (fp32) slice with
-// 16-byte loads, and every 8-lane group keeps U rows in flight.
+// load; each lane moves its 32-byte (bf16) or 64-byte (fp32) share of a row
+// with 16-byte loads (interleaved words, see raw_load), and every 8-lane
+// group keeps U rows in flight.
 // ---------------------------------------------------------------------------
 template <int DT, int EPL>
 struct RawSlice {
@@ -185,12 +190,42 @@ struct RawSlice {
   uint4 w[NW];
 };
 
+// Lane li of an 8-lane group holds the row's 16-byte words li, 8 + li,
+// 16 + li, ...: load k of the four groups of a warp reads 128 contiguous
+// bytes of each of its four rows, one cache line per row per load (a
+// contiguous 32-byte slice per lane would touch two lines per row per load).
 template <int DT, int EPL>
-__device__ __forceinline__ void raw_load(const void* row, int e0, RawSlice<DT, EPL>& r) {
-  const uint4* p = reinterpret_cast<const uint4*>(static_cast<const char*>(row) +
-                                                  (size_t)e0 * (DT == kDtF32 ? 4 : 2));
+__device__ __forceinline__ void raw_load(const void* row, int li, RawSlice<DT, EPL>& r) {
+  const uint4* p = static_cast<const uint4*>(row);
 #pragma unroll
-  for (int k = 0; k < RawSlice<DT, EPL>::NW; ++k) r.w[k] = __ldg(p + k);
+  for (int k = 0; k < RawSlice<DT, EPL>::NW; ++k) r.w[k] = __ldg(p + k * 8 + li);
+}
+
+// Row element of lane li's slice element c (the word layout of raw_load).
+template <int DT, int EPL>
+__device__ __forceinline__ int raw_elem(int li, int c) {
+  constexpr int EW = DT == kDtF32 ? 4 : 8;  // elements per 16-byte word
+  return ((c / EW) * 8 + li) * EW + c % EW;
+}
+
+// Stores lane li's slice (the word layout of raw_load) with 16-byte stores;
+// bf16 values are rounded to nearest even.
+template <int DT, int EPL>
+__device__ __forceinline__ void raw_store(void* row, int li, const float* v) {
+  uint4* p = static_cast<uint4*>(row);
+#pragma unroll
+  for (int k = 0; k < RawSlice<DT, EPL>::NW; ++k) {
+    uint4 w;
+    if constexpr (DT == kDtF32) {
+      w = make_uint4(__float_as_uint(v[4 * k]), __float_as_uint(v[4 * k + 1]), __float_as_uint(v[4 * k + 2]),
+                     __float_as_uint(v[4 * k + 3]));
+    } else {
+      const float* x = v + 8 * k;
+      auto pk = [](float lo, float hi) { return (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16); };
+      w = make_uint4(pk(x[0], x[1]), pk(x[2], x[3]), pk(x[4], x[5]), pk(x[6], x[7]));
+    }
+    p[k * 8 + li] = w;
+  }
 }
 
 template <int DT, int EPL>
@@ -268,7 +303,7 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? (DT == kDtF32 ? 2 : 4) : 4))
   const int Kp = (a.Kn + 31) & ~31;
   float* s = s_all + warp * 2 * Kp;
   int* sk = reinterpret_cast<int*>(s + Kp);
-  const int grp = lane >> 3, li = lane & 7, e0 = li * EPL;
+  const int grp = lane >> 3, li = lane & 7;
   const int64_t row = ((int64_t)b * a.H + h) * a.N + n;
   const void* nbr = static_cast<const char*>(a.nb) + row * a.Kn * (int64_t)sizeof(IT);
   const uint8_t* vr = a.valid + row * a.Kn;
@@ -277,7 +312,7 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? (DT == kDtF32 ? 2 : 4) : 4))
 
   for (int j = lane; j < a.Kn; j += 32) sk[j] = slot_ok<IT>(a, nbr, vr, j) ? load_nb<IT>(nbr, j) : -1;
   RawSlice<DT, EPL> qr;
-  raw_load<DT, EPL>(row_ptr<DT>(a.q, b * a.q_sb + h * a.q_sh + (int64_t)n * a.q_sn), e0, qr);
+  raw_load<DT, EPL>(row_ptr<DT>(a.q, b * a.q_sb + h * a.q_sh + (int64_t)n * a.q_sn), li, qr);
   unsigned long long q2[EPL / 2];
 #pragma unroll
   for (int c = 0; c < EPL / 2; ++c) q2[c] = raw_pair<DT, EPL>(qr, c);
@@ -290,7 +325,7 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? (DT == kDtF32 ? 2 : 4) : 4))
     for (int u = 0; u < U; ++u) {
       const int j = j0 + u * 4 + grp;
       const int key = j < a.Kn ? sk[j] : -1;
-      if (key >= 0) raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), e0, kr[u]);
+      if (key >= 0) raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), li, kr[u]);
       else raw_zero<DT, EPL>(kr[u]);
     }
 #pragma unroll
@@ -320,11 +355,15 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? (DT == kDtF32 ? 2 : 4) : 4))
 #pragma unroll
   for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   float sum = 0.f;
-  for (int j = lane; j < a.Kn; j += 32) sum += expf(s[j] - mx);
+  for (int j = lane; j < a.Kn; j += 32) {
+    const float e = expf(s[j] - mx);
+    s[j] = e;
+    sum += e;
+  }
 #pragma unroll
   for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   for (int j = lane; j < a.Kn; j += 32) {
-    float p = expf(s[j] - mx) / sum;
+    float p = s[j] / sum;
     if (DT == kDtBF16 && !FP32W) p = round_bf16(p);  // attn.to(v.dtype) (:1190)
     if (a.drop_thresh) {  // F.dropout(attn, p) (:1193-1194), in the weights' dtype
       const bool keep = dropout_keep((unsigned long long)row * a.Kn + j, a.drop_seed, a.drop_offset,
@@ -351,7 +390,7 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? (DT == kDtF32 ? 2 : 4) : 4))
       const int j = j0 + u * 4 + grp;
       const int key = j < a.Kn ? sk[j] : -1;
       p[u] = key >= 0 ? s[j] : 0.f;
-      if (key >= 0) raw_load<DT, EPL>(row_ptr<DT>(vb, (int64_t)key * a.v_sm), e0, vrw[u]);
+      if (key >= 0) raw_load<DT, EPL>(row_ptr<DT>(vb, (int64_t)key * a.v_sm), li, vrw[u]);
       else raw_zero<DT, EPL>(vrw[u]);
     }
 #pragma unroll
@@ -377,11 +416,7 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? (DT == kDtF32 ? 2 : 4) : 4))
     acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], 8);
     acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], 16);
   }
-  if (grp == 0) {
-    void* orow = row_ptr_mut<DT>(a.out, b * a.o_sb + h * a.o_sh + (int64_t)n * a.o_sn);
-#pragma unroll
-    for (int c = 0; c < EPL; ++c) store1<DT>(orow, e0 + c, acc[c]);
-  }
+  if (grp == 0) raw_store<DT, EPL>(row_ptr_mut<DT>(a.out, b * a.o_sb + h * a.o_sh + (int64_t)n * a.o_sn), li, acc);
   if (a.lse && lane == 0) a.lse[row] = mx + logf(sum);
 }
 
@@ -514,7 +549,7 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? 2 : 3)) k_attn_bwd_rows_v16(
   float* sp = s_all + warp * 3 * Kp;  // p_j
   float* sdp = sp + Kp;                // dP_j, then scale * dS_j
   int* sk = reinterpret_cast<int*>(sdp + Kp);
-  const int grp = lane >> 3, li = lane & 7, e0 = li * EPL;
+  const int grp = lane >> 3, li = lane & 7;
   const int64_t row = ((int64_t)b * a.H + h) * a.N + n;
   const void* nbr = static_cast<const char*>(a.nb) + row * a.Kn * (int64_t)sizeof(IT);
   const uint8_t* vr = a.valid + row * a.Kn;
@@ -524,8 +559,8 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? 2 : 3)) k_attn_bwd_rows_v16(
 
   for (int j = lane; j < a.Kn; j += 32) sk[j] = slot_ok<IT>(a, nbr, vr, j) ? load_nb<IT>(nbr, j) : -1;
   RawSlice<DT, EPL> qr, gr;
-  raw_load<DT, EPL>(row_ptr<DT>(a.q, b * a.q_sb + h * a.q_sh + (int64_t)n * a.q_sn), e0, qr);
-  raw_load<DT, EPL>(row_ptr<DT>(a.dO, orow_off), e0, gr);
+  raw_load<DT, EPL>(row_ptr<DT>(a.q, b * a.q_sb + h * a.q_sh + (int64_t)n * a.q_sn), li, qr);
+  raw_load<DT, EPL>(row_ptr<DT>(a.dO, orow_off), li, gr);
   unsigned long long q2[EPL / 2], g2[EPL / 2];
 #pragma unroll
   for (int c = 0; c < EPL / 2; ++c) {
@@ -541,8 +576,8 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? 2 : 3)) k_attn_bwd_rows_v16(
       const int j = j0 + u * 4 + grp;
       const int key = j < a.Kn ? sk[j] : -1;
       if (key >= 0) {
-        raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), e0, kr[u]);
-        raw_load<DT, EPL>(row_ptr<DT>(vb, (int64_t)key * a.v_sm), e0, vrw[u]);
+        raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), li, kr[u]);
+        raw_load<DT, EPL>(row_ptr<DT>(vb, (int64_t)key * a.v_sm), li, vrw[u]);
       } else {
         raw_zero<DT, EPL>(kr[u]);
         raw_zero<DT, EPL>(vrw[u]);
@@ -617,7 +652,7 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? 2 : 3)) k_attn_bwd_rows_v16(
       const int j = j0 + u * 4 + grp;
       const int key = j < a.Kn ? sk[j] : -1;
       ds[u] = key >= 0 ? sdp[j] : 0.f;
-      if (key >= 0) raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), e0, kr[u]);
+      if (key >= 0) raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), li, kr[u]);
       else raw_zero<DT, EPL>(kr[u]);
     }
 #pragma unroll
@@ -638,7 +673,7 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? 2 : 3)) k_attn_bwd_rows_v16(
   if (grp == 0) {
     void* dqr = row_ptr_mut<DT>(a.dq, orow_off);
 #pragma unroll
-    for (int c = 0; c < EPL; ++c) store1<DT>(dqr, e0 + c, acc[c]);
+    for (int c = 0; c < EPL; ++c) store1<DT>(dqr, raw_elem<DT, EPL>(li, c), acc[c]);
   }
 }
 
@@ -1008,7 +1043,9 @@ static cudaError_t fwd_t(const AttnDev& a, cudaStream_t st) {
   const int Kp = (a.Kn + 31) & ~31;
   // bf16 slices under 16 bytes, and head dims above 128: scalar kernel only
   if constexpr (!(DT == kDtBF16 && EPL < 8) && EPL <= 16) {
-    if (fwd_vec16_ok<DT, EPL>(a)) {
+    // the output rows are written with 16-byte stores as well
+    if (fwd_vec16_ok<DT, EPL>(a) && (reinterpret_cast<uintptr_t>(a.out) % 16) == 0 &&
+        ((a.o_sb | a.o_sh | a.o_sn) * (DT == kDtF32 ? 4 : 2)) % 16 == 0) {
       const size_t smem = (size_t)8 * 2 * Kp * sizeof(float);
       auto fn = k_attn_fwd_v16<DT, EPL, FP32W, IT>;
       cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -290,9 +290,9 @@ __global__ void __launch_bounds__(tc::THREADS, P == 1 ? 2 : 1)
       if (lane < 16) padtiles[lane] = 0u;
       __syncwarp();
       for (int r = lane; r < g.R; r += 32) {
-        const int P = (int)(g.pmax[bg * g.R + r] & 0xFFFFFu);
-        pads[r] = P;
-        atomicOr(&padtiles[(P >> 7) >> 5], 1u << ((P >> 7) & 31));
+        const int pk = (int)(g.pmax[bg * g.R + r] & 0xFFFFFu);
+        pads[r] = pk;
+        atomicOr(&padtiles[(pk >> 7) >> 5], 1u << ((pk >> 7) & 31));
       }
     }
     asm volatile("bar.sync 1, 256;" ::: "memory");  // both groups see the offsets (and pad keys)
