@@ -714,8 +714,16 @@ def run_e2e(args, job, dev, flush, world):
             while w.B * parts < args.e2e_chunks and w.n_kv % (parts * 2) == 0:
                 parts *= 2
             gp = w.n_kv // parts
-            views = [slice_views(job.q, job.k, job.v, GroupSlice(b, b + 1, g0, g0 + gp), rep)
-                     for b in range(w.B) for g0 in range(0, w.n_kv, gp)]
+            spans = [(b, g0, g0 + gp) for b in range(w.B) for g0 in range(0, w.n_kv, gp)]
+            # Tapered ends: the first chunk's copy-in and the last chunk's
+            # copy-out overlap no compute, so one kv head is split off the
+            # front of the first chunk and off the back of the last one.
+            if gp > 1:
+                b, g0, g1 = spans[0]
+                spans[0:1] = [(b, g0, g0 + 1), (b, g0 + 1, g1)]
+                b, g0, g1 = spans[-1]
+                spans[-1:] = [(b, g0, g1 - 1), (b, g1 - 1, g1)]
+            views = [slice_views(job.q, job.k, job.v, GroupSlice(b, b + 1, g0, g1), rep) for b, g0, g1 in spans]
         chunks = [tuple(pin(t.transpose(1, 2)) for t in vw) for vw in views]      # (b, N|M, heads, d)
     outs_h = [torch.empty((c[0].shape[0], c[0].shape[1], w.H if job.plan == "rows" else c[0].shape[2], w.d),
                           dtype=job.q.dtype).pin_memory() for c in chunks]
