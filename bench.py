@@ -58,7 +58,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-chunks", type=int, default=8,
-                    help="e2e: at least this many pipeline chunks where the kv heads split evenly")
+                    help="e2e: split the rank's (batch, kv-head) slices into about this many pipeline "
+                         "chunks (halving kv-head ranges down to two heads), with tapered first and last chunks")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the workload's batch size (profiling a smaller case)")
     ap.add_argument("--shard", default="auto", choices=["auto", "groups", "rows"],
@@ -683,12 +684,32 @@ def run_gpu(args):
     return result
 
 
+def e2e_spans(slices, target):
+    """Pipeline chunks of the end-to-end step as (batch, kv0, kv1) spans of
+    one batch element each: the rank's slices per batch element, halved
+    (all together) while there are fewer than `target` chunks and every
+    span keeps at least two kv heads; then one kv head is split off the
+    front of the first chunk and off the back of the last one, since only
+    the first copy-in and the last copy-out overlap no compute."""
+    spans = [(b, s.g0, s.g1) for s in slices for b in range(s.b0, s.b1)]
+    while len(spans) < target and all((g1 - g0) % 2 == 0 and g1 - g0 >= 4 for _, g0, g1 in spans):
+        spans = [(b, g, g + (g1 - g0) // 2) for b, g0, g1 in spans for g in (g0, g0 + (g1 - g0) // 2)]
+    if spans and spans[0][2] - spans[0][1] > 1:
+        b, g0, g1 = spans[0]
+        spans[0:1] = [(b, g0, g0 + 1), (b, g0 + 1, g1)]
+    if spans and spans[-1][2] - spans[-1][1] > 1:
+        b, g0, g1 = spans[-1]
+        spans[-1:] = [(b, g0, g1 - 1), (b, g1 - 1, g1)]
+    return spans
+
+
 def run_e2e(args, job, dev, flush, world):
     """The same step through the public API from pinned host memory: this
     rank's inputs copied in, its outputs copied back, inside the timing.
-    The step is cut into chunks (batch elements, or group slices); chunk i+1
-    is copied in on one stream while chunk i computes, and results go back
-    on a third stream, so PCIe transfers overlap the kernels."""
+    The step is cut into chunks (e2e_spans: kv-head ranges of one batch
+    element); chunk i+1 is copied in on one stream while chunk i computes,
+    and results go back on a third stream, so PCIe transfers overlap the
+    kernels."""
     import torch
     import torch.distributed as dist
     from ssa_b200.sharding import GroupSlice, slice_views
@@ -704,26 +725,9 @@ def run_e2e(args, job, dev, flush, world):
     if job.plan == "rows":
         chunks = [(pin(job.q.transpose(1, 2)), pin(job.k_seq), pin(job.v_seq))]   # (B,n,H,d), (m,B,n_kv,d)
     else:
-        if job.plan == "groups":
-            views = [slice_views(job.q, job.k, job.v, s, rep) for s in job.slices]
-        else:
-            # At least --e2e-chunks chunks where the kv heads split evenly: a
-            # batch element's kv-head groups in equal parts (a shorter
-            # pipeline fill and drain than one chunk per batch element).
-            parts = 1
-            while w.B * parts < args.e2e_chunks and w.n_kv % (parts * 2) == 0:
-                parts *= 2
-            gp = w.n_kv // parts
-            spans = [(b, g0, g0 + gp) for b in range(w.B) for g0 in range(0, w.n_kv, gp)]
-            # Tapered ends: the first chunk's copy-in and the last chunk's
-            # copy-out overlap no compute, so one kv head is split off the
-            # front of the first chunk and off the back of the last one.
-            if gp > 1:
-                b, g0, g1 = spans[0]
-                spans[0:1] = [(b, g0, g0 + 1), (b, g0 + 1, g1)]
-                b, g0, g1 = spans[-1]
-                spans[-1:] = [(b, g0, g1 - 1), (b, g1 - 1, g1)]
-            views = [slice_views(job.q, job.k, job.v, GroupSlice(b, b + 1, g0, g1), rep) for b, g0, g1 in spans]
+        slices = job.slices if job.plan == "groups" else [GroupSlice(0, w.B, 0, w.n_kv)]
+        views = [slice_views(job.q, job.k, job.v, GroupSlice(b, b + 1, g0, g1), rep)
+                 for b, g0, g1 in e2e_spans(slices, args.e2e_chunks)]
         chunks = [tuple(pin(t.transpose(1, 2)) for t in vw) for vw in views]      # (b, N|M, heads, d)
     outs_h = [torch.empty((c[0].shape[0], c[0].shape[1], w.H if job.plan == "rows" else c[0].shape[2], w.d),
                           dtype=job.q.dtype).pin_memory() for c in chunks]
