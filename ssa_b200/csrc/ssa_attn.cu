@@ -228,12 +228,6 @@ __device__ __forceinline__ void raw_store(void* row, int li, const float* v) {
   }
 }
 
-template <int DT, int EPL>
-__device__ __forceinline__ void raw_zero(RawSlice<DT, EPL>& r) {
-#pragma unroll
-  for (int k = 0; k < RawSlice<DT, EPL>::NW; ++k) r.w[k] = make_uint4(0u, 0u, 0u, 0u);
-}
-
 // Element c of a raw slice as fp32.
 template <int DT, int EPL>
 __device__ __forceinline__ float raw_at(const RawSlice<DT, EPL>& r, int c) {
@@ -310,7 +304,9 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? (DT == kDtF32 ? 2 : 4) : 4))
   const void* kb = row_ptr<DT>(a.k, b * a.k_sb + g * a.k_sh);
   const void* vb = row_ptr<DT>(a.v, b * a.v_sb + g * a.v_sh);
 
-  for (int j = lane; j < a.Kn; j += 32) sk[j] = slot_ok<IT>(a, nbr, vr, j) ? load_nb<IT>(nbr, j) : -1;
+  // Slot keys padded to Kp with -1, so the loops below (steps of 4U <= 32)
+  // need no bound test.
+  for (int j = lane; j < Kp; j += 32) sk[j] = (j < a.Kn && slot_ok<IT>(a, nbr, vr, j)) ? load_nb<IT>(nbr, j) : -1;
   RawSlice<DT, EPL> qr;
   raw_load<DT, EPL>(row_ptr<DT>(a.q, b * a.q_sb + h * a.q_sh + (int64_t)n * a.q_sn), li, qr);
   unsigned long long q2[EPL / 2];
@@ -321,12 +317,12 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? (DT == kDtF32 ? 2 : 4) : 4))
   // Pass 1: scores.
   for (int j0 = 0; j0 < a.Kn; j0 += 4 * U) {
     RawSlice<DT, EPL> kr[U];
+    int kv[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int j = j0 + u * 4 + grp;
-      const int key = j < a.Kn ? sk[j] : -1;
-      if (key >= 0) raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), li, kr[u]);
-      else raw_zero<DT, EPL>(kr[u]);
+      kv[u] = sk[j0 + u * 4 + grp];
+      // a slot without a key reads key 0's row; its score is masked below
+      raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)max(kv[u], 0) * a.k_sm), li, kr[u]);
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -344,8 +340,7 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? (DT == kDtF32 ? 2 : 4) : 4))
       x += __shfl_xor_sync(0xffffffffu, x, 1);
       x += __shfl_xor_sync(0xffffffffu, x, 2);
       x += __shfl_xor_sync(0xffffffffu, x, 4);
-      const int j = j0 + u * 4 + grp;
-      if (li == 0 && j < a.Kn) s[j] = sk[j] >= 0 ? x * a.scale : -INFINITY;
+      if (li == 0) s[j0 + u * 4 + grp] = kv[u] >= 0 ? x * a.scale : -INFINITY;
     }
   }
   __syncwarp();
@@ -388,10 +383,11 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? (DT == kDtF32 ? 2 : 4) : 4))
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int j = j0 + u * 4 + grp;
-      const int key = j < a.Kn ? sk[j] : -1;
+      const int key = sk[j];
       p[u] = key >= 0 ? s[j] : 0.f;
-      if (key >= 0) raw_load<DT, EPL>(row_ptr<DT>(vb, (int64_t)key * a.v_sm), li, vrw[u]);
-      else raw_zero<DT, EPL>(vrw[u]);
+      // a slot without a key reads key 0's row with weight 0, as the
+      // reference's gather of its padded index does
+      raw_load<DT, EPL>(row_ptr<DT>(vb, (int64_t)max(key, 0) * a.v_sm), li, vrw[u]);
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -557,7 +553,9 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? 2 : 3)) k_attn_bwd_rows_v16(
   const void* vb = row_ptr<DT>(a.v, b * a.v_sb + g * a.v_sh);
   const int64_t orow_off = b * a.o_sb + h * a.o_sh + (int64_t)n * a.o_sn;
 
-  for (int j = lane; j < a.Kn; j += 32) sk[j] = slot_ok<IT>(a, nbr, vr, j) ? load_nb<IT>(nbr, j) : -1;
+  // Slot keys padded to Kp with -1 (the loops below need no bound test); a
+  // slot without a key reads key 0's rows, which its zero weight cancels.
+  for (int j = lane; j < Kp; j += 32) sk[j] = (j < a.Kn && slot_ok<IT>(a, nbr, vr, j)) ? load_nb<IT>(nbr, j) : -1;
   RawSlice<DT, EPL> qr, gr;
   raw_load<DT, EPL>(row_ptr<DT>(a.q, b * a.q_sb + h * a.q_sh + (int64_t)n * a.q_sn), li, qr);
   raw_load<DT, EPL>(row_ptr<DT>(a.dO, orow_off), li, gr);
@@ -573,15 +571,9 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? 2 : 3)) k_attn_bwd_rows_v16(
     RawSlice<DT, EPL> kr[U], vrw[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int j = j0 + u * 4 + grp;
-      const int key = j < a.Kn ? sk[j] : -1;
-      if (key >= 0) {
-        raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), li, kr[u]);
-        raw_load<DT, EPL>(row_ptr<DT>(vb, (int64_t)key * a.v_sm), li, vrw[u]);
-      } else {
-        raw_zero<DT, EPL>(kr[u]);
-        raw_zero<DT, EPL>(vrw[u]);
-      }
+      const int key = max(sk[j0 + u * 4 + grp], 0);
+      raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), li, kr[u]);
+      raw_load<DT, EPL>(row_ptr<DT>(vb, (int64_t)key * a.v_sm), li, vrw[u]);
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -650,10 +642,9 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? 2 : 3)) k_attn_bwd_rows_v16(
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int j = j0 + u * 4 + grp;
-      const int key = j < a.Kn ? sk[j] : -1;
+      const int key = sk[j];
       ds[u] = key >= 0 ? sdp[j] : 0.f;
-      if (key >= 0) raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), li, kr[u]);
-      else raw_zero<DT, EPL>(kr[u]);
+      raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)max(key, 0) * a.k_sm), li, kr[u]);
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
