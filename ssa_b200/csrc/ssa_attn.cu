@@ -228,6 +228,30 @@ __device__ __forceinline__ void raw_store(void* row, int li, const float* v) {
   }
 }
 
+// Reduce-scatter over an aligned 8-lane group (lane li = lane & 7): each lane
+// holds partial sums part[0..7] of eight slots; halving exchanges with lanes
+// li ^ 1, li ^ 2, li ^ 4, each lane keeping the half its bit selects, leave
+// lane li with the group's full sum of slot li -- 7 shuffles for 8 slots,
+// and the same additions in the same order as a full butterfly per slot.
+__device__ __forceinline__ float group8_reduce_scatter(const float (&part)[8], int li) {
+  const bool b0 = li & 1, b1 = li & 2, b2 = li & 4;
+  float h4[4], h2[2];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const float keep = b0 ? part[2 * t + 1] : part[2 * t];
+    const float send = b0 ? part[2 * t] : part[2 * t + 1];
+    h4[t] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+  }
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const float keep = b1 ? h4[2 * t + 1] : h4[2 * t];
+    const float send = b1 ? h4[2 * t] : h4[2 * t + 1];
+    h2[t] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  const float keep = b2 ? h2[1] : h2[0];
+  return keep + __shfl_xor_sync(0xffffffffu, b2 ? h2[0] : h2[1], 4);
+}
+
 // Element c of a raw slice as fp32.
 template <int DT, int EPL>
 __device__ __forceinline__ float raw_at(const RawSlice<DT, EPL>& r, int c) {
@@ -314,34 +338,41 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? (DT == kDtF32 ? 2 : 4) : 4))
   for (int c = 0; c < EPL / 2; ++c) q2[c] = raw_pair<DT, EPL>(qr, c);
   __syncwarp();
 
-  // Pass 1: scores.
-  for (int j0 = 0; j0 < a.Kn; j0 += 4 * U) {
-    RawSlice<DT, EPL> kr[U];
-    int kv[U];
+  // Pass 1: scores, 8 slots per lane at a time (four steps of U = 2 rows in
+  // flight per group when U = 2, two steps when U = 4), reduced over the
+  // 8-lane group with group8_reduce_scatter.
+  static_assert(8 % U == 0, "slots per block");
+  for (int jb = 0; jb < a.Kn; jb += 32) {
+    float part[8];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      kv[u] = sk[j0 + u * 4 + grp];
-      // a slot without a key reads key 0's row; its score is masked below
-      raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)max(kv[u], 0) * a.k_sm), li, kr[u]);
-    }
+    for (int st = 0; st < 8 / U; ++st) {
+      RawSlice<DT, EPL> kr[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      float xl = 0.f, xh = 0.f;
-      if constexpr (DT == kDtBF16 && SSA_ATTN_MIXED_FMA) {
-#pragma unroll
-        for (int c = 0; c < EPL / 2; ++c) bf2_fma(raw_word<DT, EPL>(qr, c), raw_word<DT, EPL>(kr[u], c), xl, xh);
-      } else {
-        unsigned long long x2 = 0ull;
-#pragma unroll
-        for (int c = 0; c < EPL / 2; ++c) x2 = f2_fma(q2[c], raw_pair<DT, EPL>(kr[u], c), x2);
-        f2_unpack(x2, xl, xh);
+      for (int u = 0; u < U; ++u) {
+        // a slot without a key reads key 0's row; its score is masked below
+        const int key = max(sk[jb + (st * U + u) * 4 + grp], 0);
+        raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), li, kr[u]);
       }
-      float x = xl + xh;
-      x += __shfl_xor_sync(0xffffffffu, x, 1);
-      x += __shfl_xor_sync(0xffffffffu, x, 2);
-      x += __shfl_xor_sync(0xffffffffu, x, 4);
-      if (li == 0) s[j0 + u * 4 + grp] = kv[u] >= 0 ? x * a.scale : -INFINITY;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float xl = 0.f, xh = 0.f;
+        if constexpr (DT == kDtBF16 && SSA_ATTN_MIXED_FMA) {
+#pragma unroll
+          for (int c = 0; c < EPL / 2; ++c) bf2_fma(raw_word<DT, EPL>(qr, c), raw_word<DT, EPL>(kr[u], c), xl, xh);
+        } else {
+          unsigned long long x2 = 0ull;
+#pragma unroll
+          for (int c = 0; c < EPL / 2; ++c) x2 = f2_fma(q2[c], raw_pair<DT, EPL>(kr[u], c), x2);
+          f2_unpack(x2, xl, xh);
+        }
+        part[st * U + u] = xl + xh;
+      }
     }
+    // slot m of the block (part[m]) is j = jb + m * 4 + grp; lane li ends
+    // with slot li (sk and s hold Kp entries, a multiple of 32)
+    const float x = group8_reduce_scatter(part, li);
+    const int js = jb + li * 4 + grp;
+    s[js] = sk[js] >= 0 ? x * a.scale : -INFINITY;
   }
   __syncwarp();
   // Softmax in fp32 (:1167).
@@ -567,38 +598,42 @@ __global__ void __launch_bounds__(256, (EPL >= 16 ? 2 : 3)) k_attn_bwd_rows_v16(
   }
   const float lse = a.lse_in[row];
   __syncwarp();
-  for (int j0 = 0; j0 < a.Kn; j0 += 4 * U) {
-    RawSlice<DT, EPL> kr[U], vrw[U];
+  // 8 slots per lane at a time (four steps of U = 2 rows in flight per
+  // group), p and dP reduced over the 8-lane group with
+  // group8_reduce_scatter: lane li ends with slot li of the block.
+  static_assert(8 % U == 0, "slots per block");
+  for (int jb = 0; jb < a.Kn; jb += 32) {
+    float ps8[8], pd8[8];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int key = max(sk[j0 + u * 4 + grp], 0);
-      raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), li, kr[u]);
-      raw_load<DT, EPL>(row_ptr<DT>(vb, (int64_t)key * a.v_sm), li, vrw[u]);
-    }
+    for (int st = 0; st < 8 / U; ++st) {
+      RawSlice<DT, EPL> kr[U], vrw[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      unsigned long long x2 = 0ull, y2 = 0ull;
-#pragma unroll
-      for (int c = 0; c < EPL / 2; ++c) {
-        x2 = f2_fma(q2[c], raw_pair<DT, EPL>(kr[u], c), x2);
-        y2 = f2_fma(g2[c], raw_pair<DT, EPL>(vrw[u], c), y2);
+      for (int u = 0; u < U; ++u) {
+        const int key = max(sk[jb + (st * U + u) * 4 + grp], 0);
+        raw_load<DT, EPL>(row_ptr<DT>(kb, (int64_t)key * a.k_sm), li, kr[u]);
+        raw_load<DT, EPL>(row_ptr<DT>(vb, (int64_t)key * a.v_sm), li, vrw[u]);
       }
-      float xl, xh, yl, yh;
-      f2_unpack(x2, xl, xh);
-      f2_unpack(y2, yl, yh);
-      float ps = xl + xh, pd = yl + yh;
 #pragma unroll
-      for (int o = 1; o < 8; o <<= 1) {
-        ps += __shfl_xor_sync(0xffffffffu, ps, o);
-        pd += __shfl_xor_sync(0xffffffffu, pd, o);
-      }
-      const int j = j0 + u * 4 + grp;
-      if (li == 0 && j < a.Kn) {
-        const bool ok = sk[j] >= 0;
-        sp[j] = ok ? expf(ps * a.scale - lse) : 0.f;
-        sdp[j] = ok ? pd : 0.f;
+      for (int u = 0; u < U; ++u) {
+        unsigned long long x2 = 0ull, y2 = 0ull;
+#pragma unroll
+        for (int c = 0; c < EPL / 2; ++c) {
+          x2 = f2_fma(q2[c], raw_pair<DT, EPL>(kr[u], c), x2);
+          y2 = f2_fma(g2[c], raw_pair<DT, EPL>(vrw[u], c), y2);
+        }
+        float xl, xh, yl, yh;
+        f2_unpack(x2, xl, xh);
+        f2_unpack(y2, yl, yh);
+        ps8[st * U + u] = xl + xh;
+        pd8[st * U + u] = yl + yh;
       }
     }
+    const float ps = group8_reduce_scatter(ps8, li);
+    const float pd = group8_reduce_scatter(pd8, li);
+    const int j = jb + li * 4 + grp;  // sp / sdp hold Kp entries; slots past Kn have no key
+    const bool ok = sk[j] >= 0;
+    sp[j] = ok ? expf(ps * a.scale - lse) : 0.f;
+    sdp[j] = ok ? pd : 0.f;
   }
   __syncwarp();
   // Dropout: the gradient reaching the pre-dropout weights is dO.v_j scaled
